@@ -1,0 +1,299 @@
+/*
+ * spmvb200.h — C ABI of libspmvb200.so, a CSR sparse matrix-vector product (y = A x) for NVIDIA B200
+ * (sm_100a) with compressed column indices.
+ *
+ * It is a drop-in for the hot path of the spmv-index-compression study (HERMES-TorVerLab/
+ * spmv-index-compression): the CSR reader, RCM reordering and characterization of include/csr.hpp,
+ * include/rcm.hpp and src/characterize_matrix.cpp, the layout encoders and byte model of
+ * src/bench_csr_width.cu:149-285 and :795-960, and the kernels and dispatch of
+ * src/bench_csr_width.cu:287-629. Every declaration below names the reference interface it replaces.
+ * That program has no library interface of its own; its de facto operator surface is
+ * launch<T>(threads_per_row, Configuration, DeviceMatrix<T>) (bench_csr_width.cu:607).
+ *
+ * Conventions
+ *   - Every function returns SPMV_OK (0) or a positive SPMV_ERR_* status; the reference calls exit()
+ *     on any CUDA error (include/common.cuh:19-27), this library returns the status instead and keeps
+ *     a message for spmv_last_error().
+ *   - Layouts: CSR-i32, CSR-i16 (16-bit absolute), CSR-r16 (16-bit offset from the row's first column),
+ *     CSR-lp (per-lane bit-packed difference chains), and the 8-bit i8/r8 of the same families.
+ *   - threads per row T is in {2, 4, 8, 16, 32}; results are bit-identical to the reference CSR-i32
+ *     kernel at the same T (same nonzero order, lane striding and shuffle-reduction order).
+ *   - Value types FP64, FP32, FP16; FP16 accumulates in FP32 (include/value_types.cuh:9-13).
+ *   - Ownership: the library owns the encoded operator buffers; the caller owns x and y.
+ *     An operator may be used from several host threads as long as each call has its own stream
+ *     and y; calls on one operator never write to the operator.
+ *   - Streams are passed as void* (a cudaStream_t, NULL for the legacy default stream), so this header
+ *     needs no CUDA include.
+ */
+#ifndef SPMVB200_H
+#define SPMVB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status ----------------------------------------------------------------------------------- */
+#define SPMV_OK 0
+#define SPMV_ERR_INVALID_ARGUMENT 1
+#define SPMV_ERR_IO 2                /* a file could not be opened, read or written */
+#define SPMV_ERR_FORMAT 3            /* malformed Matrix Market or permutation file */
+#define SPMV_ERR_NOT_ADMISSIBLE 4    /* the layout cannot represent this matrix exactly */
+#define SPMV_ERR_OUT_OF_MEMORY 5     /* host or device allocation failed */
+#define SPMV_ERR_CUDA 6              /* a CUDA runtime call failed */
+#define SPMV_ERR_UNSUPPORTED 7       /* e.g. no CUDA device, or a library that is missing */
+#define SPMV_ERR_NCCL 8              /* an NCCL call failed or NCCL could not be loaded */
+#define SPMV_ERR_TIMEOUT 9           /* a bounded device-side wait gave up (see spmv_operator_check) */
+#define SPMV_ERR_TOO_LARGE 10        /* a size exceeds a documented limit */
+
+/* ---- enums -------------------------------------------------------------------------------------- */
+/* Column layouts (the Configuration of bench_csr_width.cu:88 as column_mode x column_bytes). */
+#define SPMV_LAYOUT_I32 0   /* absolute, 4 bytes                              */
+#define SPMV_LAYOUT_I16 1   /* absolute, 2 bytes: admissible iff cols <= 2^16  */
+#define SPMV_LAYOUT_R16 2   /* row-base, 2-byte offsets: every row spans < 2^16 */
+#define SPMV_LAYOUT_LP  3   /* lane-packed difference chains (depends on T)   */
+#define SPMV_LAYOUT_I8  4   /* absolute, 1 byte: cols <= 256                   */
+#define SPMV_LAYOUT_R8  5   /* row-base, 1-byte offsets: every row spans < 256 */
+
+/* Value types (PrecisionName, include/value_types.cuh:37-40). */
+#define SPMV_F64 0
+#define SPMV_F32 1
+#define SPMV_F16 2
+
+/* ---- library ------------------------------------------------------------------------------------ */
+const char* spmv_version(void);
+const char* spmv_status_string(int status);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* spmv_last_error(void);
+
+/* ---- host CSR matrix: CsrMatrix (include/csr.hpp:33) -------------------------------------------- */
+typedef struct spmv_csr spmv_csr;
+
+/* MatrixStats (include/csr.hpp:22) plus the shape. */
+typedef struct {
+  int rows;
+  int cols;
+  int64_t nnz;
+  double nnz_per_row_mean;
+  int nnz_per_row_max;
+  int nnz_per_row_min;
+  double nnz_per_row_std;
+  double dynamic_range;
+  double norm_inf;
+  double max_abs;
+  double min_abs;
+  int symmetric_expanded;
+} spmv_csr_info;
+
+/* read_matrix_market (include/csr.hpp:232): coordinate real/integer/pattern, general/symmetric/
+ * skew-symmetric/hermitian, symmetric files expanded, columns sorted within rows, stats computed.
+ * Errors: SPMV_ERR_IO (cannot open), SPMV_ERR_FORMAT (not Matrix Market, not coordinate, bad size). */
+int spmv_csr_read_matrix_market(const char* path, spmv_csr** out);
+
+/* A CsrMatrix from caller arrays (copied). Columns are sorted within rows as sort_columns_within_rows
+ * (include/csr.hpp:162) does and the stats are computed (CsrMatrix::compute_stats, csr.hpp:43).
+ * values may be NULL (all 1.0). name may be NULL. nnz = row_ptr[rows] must fit int32, as in the
+ * reference. */
+int spmv_csr_create(int rows, int cols, const int* row_ptr, const int* col_ind, const double* values,
+                    const char* name, spmv_csr** out);
+int spmv_csr_get_info(const spmv_csr* matrix, spmv_csr_info* info);
+/* Borrowed pointers to the host arrays, valid until spmv_csr_destroy. */
+int spmv_csr_get_arrays(const spmv_csr* matrix, const int** row_ptr, const int** col_ind, const double** values);
+const char* spmv_csr_name(const spmv_csr* matrix);
+int spmv_csr_set_name(spmv_csr* matrix, const char* name);
+void spmv_csr_destroy(spmv_csr* matrix);
+
+/* Rows [row_begin, row_end) as a matrix of their own with all columns kept (a row shard). */
+int spmv_csr_slice_rows(const spmv_csr* matrix, int row_begin, int row_end, spmv_csr** out);
+
+/* ---- RCM ordering: include/rcm.hpp -------------------------------------------------------------- */
+/* reverse_cuthill_mckee (rcm.hpp:199): new_to_old[rows]; square matrices only. */
+int spmv_rcm_order(const spmv_csr* matrix, int* new_to_old);
+/* apply_symmetric_permutation (rcm.hpp:219): B = P A P^T, columns re-sorted, stats recomputed. */
+int spmv_csr_permute(const spmv_csr* matrix, const int* new_to_old, spmv_csr** out);
+/* permutation_path_for (rcm.hpp:244): "<stem>.<ordering>.perm". Writes at most cap bytes with the NUL. */
+int spmv_permutation_path(const char* matrix_path, const char* ordering, char* out, size_t cap);
+/* write_permutation (rcm.hpp:250): magic "RCMPERM1", int64 rows, double seconds, int32 new_to_old;
+ * written to "<path>.partial" and renamed. */
+int spmv_permutation_write(const char* path, const int* new_to_old, int64_t rows, double seconds);
+/* read_permutation (rcm.hpp:274): *found = 0 when the file does not exist; SPMV_ERR_FORMAT when it
+ * exists but is not a valid permutation of expected_rows entries. */
+int spmv_permutation_read(const char* path, int expected_rows, int* new_to_old, double* seconds, int* found);
+/* reorder_with_rcm (rcm.hpp:306): loads <stem>.rcm.perm beside matrix_path, or computes and saves it;
+ * returns P A P^T and the seconds the ordering took when it was computed. */
+int spmv_csr_reorder_rcm(const char* matrix_path, const spmv_csr* matrix, spmv_csr** out, double* seconds);
+
+/* ---- characterization: src/characterize_matrix.cpp ---------------------------------------------- */
+/* The 60-column CSV of write_csv (characterize_matrix.cpp:253), header line and value line, for the
+ * FP64 byte model. ordering is "original" or "rcm". *needed receives the bytes required (with NUL);
+ * SPMV_ERR_TOO_LARGE if cap is smaller. Requires a square matrix with nnz > 0 (characterize main:314). */
+int spmv_characterize(const spmv_csr* matrix, const char* ordering, double ordering_seconds, char* csv,
+                      size_t cap, size_t* needed);
+
+/* ---- layouts, admissibility and byte model: src/bench_csr_width.cu:149-285 ------------------------ */
+/* MatrixFacts (bench_csr_width.cu:160): widest row span and the CSR-lp word counts by log2(T). */
+typedef struct {
+  int widest_row_span;
+  int64_t lane_packed_words[6];   /* [log2 T], T = 2..32 in slots 1..5, each including the 2 spare words */
+} spmv_facts;
+
+/* MemoryBreakdown (bench_csr_width.cu:95): bytes of every stream one product touches. */
+typedef struct {
+  double values;
+  double columns;
+  double column_bases;
+  double row_pointer;
+  double vectors;
+  double total;
+} spmv_memory;
+
+/* facts_of (bench_csr_width.cu:223). */
+int spmv_matrix_facts(const spmv_csr* matrix, spmv_facts* facts);
+/* configuration_admissible (bench_csr_width.cu:246); tpr matters for CSR-lp only (0 means 8). */
+int spmv_admissible(const spmv_csr* matrix, const spmv_facts* facts, int layout, int tpr, int* admissible);
+/* memory_of (bench_csr_width.cu:258); tpr matters for CSR-lp only (0 means 8). */
+int spmv_memory_of(const spmv_csr* matrix, const spmv_facts* facts, int layout, int dtype, int tpr, spmv_memory* memory);
+
+/* Host encoders, producing the reference's exact streams.
+ * upload_columns<T, I> (bench_csr_width.cu:796): absolute columns narrowed to 2 (i16) or 1 (i8) bytes. */
+int spmv_encode_absolute(const spmv_csr* matrix, int column_bytes, void* columns);
+/* upload_row_bases (bench_csr_width.cu:807): first column of each row, 0 for an empty row. */
+int spmv_encode_row_base(const spmv_csr* matrix, int* row_base);
+/* upload_relative_columns<I> (bench_csr_width.cu:820): col - row base in 2 (r16) or 1 (r8) bytes. */
+int spmv_encode_relative(const spmv_csr* matrix, int column_bytes, void* offsets);
+/* packed_word_count (bench_csr_width.cu:206). */
+int spmv_lane_packed_word_count(const spmv_csr* matrix, int tpr, int64_t* word_count);
+/* build_packed_deltas (bench_csr_width.cu:861): row_word[rows], row_width[rows], words[word_count]. */
+int spmv_encode_lane_packed(const spmv_csr* matrix, int tpr, int64_t word_count, int* row_word, uint8_t* row_width,
+                            uint32_t* words);
+
+/* ---- device operator: DeviceMatrix<T> + Configuration (bench_csr_width.cu:88, :128) ------------- */
+typedef struct spmv_operator spmv_operator;
+
+typedef struct {
+  int layout;
+  int dtype;
+  int tpr;                /* T: threads per row of the summation order, 2..32                       */
+  int physical_tpr;       /* threads of the kernel per row, dividing T (0 = chosen by the library)  */
+  int tile_nnz;           /* nonzeros staged per tile (0 = default)                                  */
+  int value_rounding;     /* 0: values (T)(float)val as upload_matrix does (:927); 1: (T)val          */
+  int device;             /* CUDA device ordinal (-1 = current device)                               */
+} spmv_operator_config;
+
+/* Fills a config with defaults: physical_tpr 0, tile_nnz 0, value_rounding 0, device -1. */
+void spmv_operator_config_init(spmv_operator_config* config, int layout, int dtype, int tpr);
+
+/* upload_matrix + upload_* (bench_csr_width.cu:795-951): encodes the matrix in the layout, converts
+ * the values, plans the tiles and uploads everything to the device. SPMV_ERR_NOT_ADMISSIBLE when the
+ * layout cannot hold the matrix exactly (reported as "not admissible" by the reference, :1198). */
+int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* config, spmv_operator** out);
+
+typedef struct {
+  int rows;
+  int cols;
+  int64_t nnz;
+  int layout;
+  int dtype;
+  int tpr;
+  int physical_tpr;
+  int tile_nnz;
+  int64_t tiles;             /* staged tiles of short rows                                   */
+  int64_t long_rows;         /* rows longer than a tile, streamed by the long-row path       */
+  int64_t device_bytes;      /* bytes of device memory the operator holds                    */
+  spmv_memory memory;        /* memory_of of this layout at this T (algorithmic bytes/product) */
+} spmv_operator_info;
+int spmv_operator_get_info(const spmv_operator* op, spmv_operator_info* info);
+
+/* launch<T> (bench_csr_width.cu:607): y = A x on the given stream, x and y device pointers of the
+ * operator's value type (x: cols entries, y: rows entries). Asynchronous; launch errors are returned. */
+int spmv_operator_run(const spmv_operator* op, const void* x, void* y, void* stream);
+/* The same product through host buffers: copies x to the device, multiplies, copies y back and waits
+ * (result_at_fixed_tpr, bench_csr_width.cu:779). x_device and y_device are caller scratch on the device. */
+int spmv_operator_run_host(const spmv_operator* op, const void* x_host, void* y_host, void* x_device, void* y_device,
+                           void* stream);
+/* Reads and clears the operator's device status word: SPMV_ERR_TIMEOUT if a bounded device-side wait
+ * gave up since the last check. Synchronises the device. */
+int spmv_operator_check(const spmv_operator* op);
+/* Device pointers of the encoded streams (for callers that launch on their own arrays). */
+typedef struct {
+  const int* row_ptr;
+  const void* columns;
+  const int* row_base;
+  const int* row_word;
+  const uint8_t* row_width;
+  const uint32_t* words;
+  const void* values;
+} spmv_operator_arrays;
+int spmv_operator_get_arrays(const spmv_operator* op, spmv_operator_arrays* arrays);
+void spmv_operator_destroy(spmv_operator* op);
+
+/* ---- raw launch over caller-owned device arrays ------------------------------------------------- */
+/* The DeviceMatrix<T> of bench_csr_width.cu:128 restricted to one layout. */
+typedef struct {
+  int rows;
+  int cols;
+  int64_t nnz;
+  const int* row_ptr;       /* int32[rows + 1]                                         */
+  const void* columns;      /* i32: int32, i16/r16: uint16, i8/r8: uint8 [nnz]; lp: unused */
+  const int* row_base;      /* r16/r8/lp: int32[rows]                                  */
+  const int* row_word;      /* lp: int32[rows]                                         */
+  const uint8_t* row_width; /* lp: uint8[rows]                                         */
+  const uint32_t* words;    /* lp: uint32[word_count], with its 2 spare words          */
+  const void* values;       /* value type [nnz]                                        */
+  const void* x;            /* value type [cols]                                       */
+  void* y;                  /* value type [rows]                                       */
+} spmv_device_matrix;
+/* launch<T> (bench_csr_width.cu:607-629) on caller arrays: one vector of T threads per row, no
+ * preprocessing and no workspace. */
+int spmv_launch(int layout, int dtype, int tpr, const spmv_device_matrix* matrix, void* stream);
+
+/* ---- synthetic matrices for the benchmark configurations ---------------------------------------- */
+/* 2D 5-point Laplacian on grid x grid (diagonal 4, neighbours -1). */
+int spmv_synth_laplacian2d(int grid, spmv_csr** out);
+/* n x n band: each row k ~ Poisson(mean) (at least 1) distinct off-diagonal columns uniform in
+ * [row - half_bandwidth, row + half_bandwidth], plus the diagonal; values N(0,1). */
+int spmv_synth_random_band(int n, int half_bandwidth, double mean, uint64_t seed, spmv_csr** out);
+/* 3D 27-point stencil on grid^3 in lexicographic order (diagonal 26, neighbours -1). */
+int spmv_synth_stencil27(int grid, spmv_csr** out);
+/* n x n power law: row lengths Zipf(alpha) clipped to [1, max_length] and rescaled to the given mean,
+ * columns uniform over [0, n) without repeats in a row, values uniform [-1, 1]. */
+int spmv_synth_power_law(int n, double alpha, int max_length, double mean, uint64_t seed, spmv_csr** out);
+/* Rows [row_begin, row_end) of an n x n block matrix of block x block dense blocks: every block row
+ * holds its diagonal block and blocks_per_row - 1 more at distinct block offsets uniform within
+ * +-offset_range rows; values N(0,1) and a diagonally dominant diagonal. Any row range can be built on
+ * its own (a shard), identical to the same rows of the whole matrix. */
+int spmv_synth_block_fem(int n, int block, int blocks_per_row, int offset_range, uint64_t seed, int row_begin,
+                         int row_end, spmv_csr** out);
+/* count values uniform in [-1, 1] from seed, stored as dtype ((T)(float)u, as the reference casts x,
+ * bench_csr_width.cu:928). The same seed gives the same values for every dtype. */
+int spmv_fill_uniform(int dtype, int64_t count, uint64_t seed, void* out);
+/* The reference's own x: std::mt19937(7), uniform_real_distribution<double>(-1, 1), cast through float
+ * (upload_matrix, bench_csr_width.cu:923-928). */
+int spmv_fill_reference_x(int dtype, int64_t count, void* out);
+
+/* ---- multi-GPU: nnz-balanced row shards, x replicated, y all-gathered into the next x ------------ */
+/* Row boundaries of nshards row blocks balanced by nonzeros: row_begin[0] = 0, row_begin[nshards] = rows. */
+int spmv_shard_rows(const spmv_csr* matrix, int nshards, int* row_begin);
+
+/* An NCCL communicator over the ranks of one job (NCCL is loaded at run time). */
+typedef struct spmv_comm spmv_comm;
+/* 128 bytes (ncclUniqueId) to be broadcast from rank 0 to the others by the caller. */
+int spmv_comm_unique_id(void* id128);
+int spmv_comm_create(int nranks, int rank, const void* id128, int device, spmv_comm** out);
+void spmv_comm_destroy(spmv_comm* comm);
+
+/* Chained products y -> x over the row shards: each rank holds the operator of its rows
+ * (shard_row_begin[rank] .. shard_row_begin[rank+1]) and the full x. Every product computes the rank's y
+ * shard into its slice of the next x, then all-gathers the slices over NCCL, products times. x_current
+ * and x_next are device buffers of cols entries (the square matrix's n); the result is left in x_current
+ * if products is even, else in x_next. All ranks must call it with the same products. */
+int spmv_chain_run(const spmv_operator* shard_op, spmv_comm* comm, const int* shard_row_begin, void* x_current,
+                   void* x_next, int products, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPMVB200_H */

@@ -1,0 +1,20 @@
+// capi_internal.hpp — error plumbing shared by the C entry points.
+#pragma once
+
+#include <functional>
+#include <memory>
+#include <string>
+
+#include "internal.hpp"
+
+namespace spmvb200 {
+
+void set_last_error(const std::string& message);
+// Runs body, returning SPMV_OK or the status of the exception it threw (message kept for spmv_last_error).
+int guarded(const std::function<void()>& body);
+// Throws SPMV_ERR_INVALID_ARGUMENT with message unless condition holds.
+void require(bool condition, const char* message);
+// The caller's facts, or facts_of(matrix) when facts is null.
+Facts facts_for(const spmv_csr* matrix, const spmv_facts* facts);
+
+}  // namespace spmvb200

@@ -1,0 +1,42 @@
+// dispatch.hpp — host entry points into the kernel instantiations (one translation unit per value type).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "kernels.cuh"
+
+namespace spmvb200 {
+
+// Physical threads per row the tile kernel is built for: P = T / S with S in {1, 2, 4, 8, 16}.
+inline bool tile_variant_exists(int tpr, int physical_tpr) {
+  if (physical_tpr < 1 || physical_tpr > tpr || tpr % physical_tpr != 0) return false;
+  const int slots = tpr / physical_tpr;
+  return slots == 1 || slots == 2 || slots == 4 || slots == 8 || slots == 16;
+}
+
+// k_spmv_tiles over a.vector_blocks + a.tile_count CTAs with the shared memory of the tile plan.
+cudaError_t launch_tiles_f64(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream);
+cudaError_t launch_tiles_f32(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream);
+cudaError_t launch_tiles_f16(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream);
+// k_spmv_vector over `blocks` CTAs of kVectorBlock threads.
+cudaError_t launch_vector_f64(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream);
+cudaError_t launch_vector_f32(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream);
+cudaError_t launch_vector_f16(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream);
+
+inline cudaError_t launch_tiles(int dtype, int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream) {
+  switch (dtype) {
+    case SPMV_F64: return launch_tiles_f64(layout, tpr, physical_tpr, a, stream);
+    case SPMV_F32: return launch_tiles_f32(layout, tpr, physical_tpr, a, stream);
+    default:       return launch_tiles_f16(layout, tpr, physical_tpr, a, stream);
+  }
+}
+
+inline cudaError_t launch_vector(int dtype, int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream) {
+  switch (dtype) {
+    case SPMV_F64: return launch_vector_f64(layout, tpr, a, blocks, stream);
+    case SPMV_F32: return launch_vector_f32(layout, tpr, a, blocks, stream);
+    default:       return launch_vector_f16(layout, tpr, a, blocks, stream);
+  }
+}
+
+}  // namespace spmvb200

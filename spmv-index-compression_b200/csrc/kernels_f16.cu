@@ -1,0 +1,5 @@
+// kernels_f16.cu — kernel instantiations for __half values.
+#define VALUE_TYPE __half
+#define LAUNCH_TILES_NAME launch_tiles_f16
+#define LAUNCH_VECTOR_NAME launch_vector_f16
+#include "kernels_instantiate.cuh"

@@ -1,0 +1,92 @@
+// kernels_instantiate.cuh — the switch from runtime (layout, T, P) to a kernel instantiation for the
+// value type VALUE_TYPE, included by kernels_f64.cu, kernels_f32.cu and kernels_f16.cu.
+#include "dispatch.hpp"
+
+namespace spmvb200 {
+namespace {
+
+template <class V, int L, int T, int P>
+cudaError_t run_tiles(const KernelArgs& a, cudaStream_t stream) {
+  const TileSmem plan = tile_smem(a.tile_nnz, a.tile_rows, (int)sizeof(V), L);
+  if (plan.total > 48 * 1024) {
+    const cudaError_t status = cudaFuncSetAttribute(k_spmv_tiles<V, L, T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.total);
+    if (status != cudaSuccess) return status;
+  }
+  const int64_t blocks = a.vector_blocks + a.tile_count;
+  if (blocks <= 0) return cudaSuccess;
+  k_spmv_tiles<V, L, T, P><<<(unsigned)blocks, kTileBlock, plan.total, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <class V, int L, int T>
+cudaError_t tiles_for_tpr(int physical_tpr, const KernelArgs& a, cudaStream_t stream) {
+  switch (T / physical_tpr) {
+    case 1: return run_tiles<V, L, T, T>(a, stream);
+    case 2: if constexpr (T >= 2) return run_tiles<V, L, T, T / 2>(a, stream); break;
+    case 4: if constexpr (T >= 4) return run_tiles<V, L, T, T / 4>(a, stream); break;
+    case 8: if constexpr (T >= 8) return run_tiles<V, L, T, T / 8>(a, stream); break;
+    case 16: if constexpr (T >= 16) return run_tiles<V, L, T, T / 16>(a, stream); break;
+    default: break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <class V, int L>
+cudaError_t tiles_for_layout(int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream) {
+  if (!tile_variant_exists(tpr, physical_tpr)) return cudaErrorInvalidValue;
+  switch (tpr) {
+    case 2: return tiles_for_tpr<V, L, 2>(physical_tpr, a, stream);
+    case 4: return tiles_for_tpr<V, L, 4>(physical_tpr, a, stream);
+    case 8: return tiles_for_tpr<V, L, 8>(physical_tpr, a, stream);
+    case 16: return tiles_for_tpr<V, L, 16>(physical_tpr, a, stream);
+    case 32: return tiles_for_tpr<V, L, 32>(physical_tpr, a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <class V, int L, int T>
+cudaError_t run_vector(const KernelArgs& a, int64_t blocks, cudaStream_t stream) {
+  if (blocks <= 0) return cudaSuccess;
+  k_spmv_vector<V, L, T><<<(unsigned)blocks, kVectorBlock, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <class V, int L>
+cudaError_t vector_for_layout(int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream) {
+  switch (tpr) {
+    case 2: return run_vector<V, L, 2>(a, blocks, stream);
+    case 4: return run_vector<V, L, 4>(a, blocks, stream);
+    case 8: return run_vector<V, L, 8>(a, blocks, stream);
+    case 16: return run_vector<V, L, 16>(a, blocks, stream);
+    case 32: return run_vector<V, L, 32>(a, blocks, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+cudaError_t LAUNCH_TILES_NAME(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream) {
+  switch (layout) {
+    case SPMV_LAYOUT_I32: return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_I32>(tpr, physical_tpr, a, stream);
+    case SPMV_LAYOUT_I16: return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_I16>(tpr, physical_tpr, a, stream);
+    case SPMV_LAYOUT_R16: return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_R16>(tpr, physical_tpr, a, stream);
+    case SPMV_LAYOUT_LP:  return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_LP>(tpr, physical_tpr, a, stream);
+    case SPMV_LAYOUT_I8:  return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_I8>(tpr, physical_tpr, a, stream);
+    case SPMV_LAYOUT_R8:  return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_R8>(tpr, physical_tpr, a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t LAUNCH_VECTOR_NAME(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream) {
+  switch (layout) {
+    case SPMV_LAYOUT_I32: return vector_for_layout<VALUE_TYPE, SPMV_LAYOUT_I32>(tpr, a, blocks, stream);
+    case SPMV_LAYOUT_I16: return vector_for_layout<VALUE_TYPE, SPMV_LAYOUT_I16>(tpr, a, blocks, stream);
+    case SPMV_LAYOUT_R16: return vector_for_layout<VALUE_TYPE, SPMV_LAYOUT_R16>(tpr, a, blocks, stream);
+    case SPMV_LAYOUT_LP:  return vector_for_layout<VALUE_TYPE, SPMV_LAYOUT_LP>(tpr, a, blocks, stream);
+    case SPMV_LAYOUT_I8:  return vector_for_layout<VALUE_TYPE, SPMV_LAYOUT_I8>(tpr, a, blocks, stream);
+    case SPMV_LAYOUT_R8:  return vector_for_layout<VALUE_TYPE, SPMV_LAYOUT_R8>(tpr, a, blocks, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace spmvb200

@@ -1,0 +1,407 @@
+// operator.cu — the device-resident operator: encode, plan tiles, upload, launch.
+//
+// Layout in HBM of one operator (one allocation per stream, each 256-byte aligned by cudaMalloc):
+//   row_ptr   int32[rows + 1]                     the CSR row pointer (all layouts)
+//   values    T[nnz]                              (T)(float)val by default, as upload_matrix (:927)
+//   columns   int32 / uint16 / uint8 [nnz]        i32, i16, i8 absolute; r16, r8 offsets from the base
+//   row_base  int32[rows]                         r16, r8, lp: the row's first column
+//   row_word  int32[rows], row_width uint8[rows]  lp: first word and bit width of the row's stream
+//   words     uint32[word_count]                  lp: lane-major packed deltas + 2 spare words
+//   tiles     int4[tiles]                         {row_begin, row_end, entry_begin, entry_end}
+//   tile_words int2[tiles]                        lp: {first word, last word + 1} of each tile's stream
+//   long_rows int32[long_rows]                    rows longer than a tile
+//   status    uint32                              bit 0: a bounded device wait gave up
+// The streams are the reference's (bench_csr_width.cu:795-951), so memory_of counts them exactly; the
+// tile plan adds 16 bytes per tile (about 2048 nonzeros) and 4 bytes per long row.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <memory>
+
+#include "capi_internal.hpp"
+#include "dispatch.hpp"
+
+namespace spmvb200 {
+
+namespace {
+
+void cuda_check(cudaError_t status, const char* what) {
+  if (status == cudaSuccess) return;
+  const int code = status == cudaErrorMemoryAllocation ? SPMV_ERR_OUT_OF_MEMORY : SPMV_ERR_CUDA;
+  fail(code, std::string(what) + ": " + cudaGetErrorString(status));
+}
+
+// Restores the caller's current device when it goes out of scope.
+struct DeviceScope {
+  int previous = -1;
+  explicit DeviceScope(int device) {
+    cuda_check(cudaGetDevice(&previous), "cudaGetDevice");
+    if (device >= 0 && device != previous) cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  }
+  ~DeviceScope() {
+    if (previous >= 0) cudaSetDevice(previous);
+  }
+};
+
+template <class T>
+T* device_upload(const void* host, size_t count, int64_t& total_bytes) {
+  T* device = nullptr;
+  if (count == 0) count = 1;   // keep every stream a valid pointer
+  cuda_check(cudaMalloc(reinterpret_cast<void**>(&device), sizeof(T) * count), "cudaMalloc");
+  total_bytes += (int64_t)(sizeof(T) * count);
+  if (host) {
+    const cudaError_t status = cudaMemcpy(device, host, sizeof(T) * count, cudaMemcpyHostToDevice);
+    if (status != cudaSuccess) {
+      cudaFree(device);
+      cuda_check(status, "cudaMemcpy");
+    }
+  }
+  return device;
+}
+
+}  // namespace
+
+// Tile plan: maximal runs of consecutive rows with at most tile_nnz nonzeros and tile_rows rows; a row
+// with more than tile_nnz nonzeros is listed as long and processed by the vector path instead.
+struct TilePlan {
+  std::vector<int4> tiles;
+  std::vector<int2> tile_words;
+  std::vector<int> long_rows;
+  int64_t short_rows = 0;
+  int64_t short_nnz = 0;
+};
+
+TilePlan plan_tiles(const Csr& matrix, int tile_nnz, int tile_rows, const int* row_word, const uint8_t* row_width) {
+  TilePlan plan;
+  int begin = -1, count = 0;
+  int64_t nnz = 0;
+  auto close = [&](int end) {
+    if (begin < 0) return;
+    plan.tiles.push_back(make_int4(begin, end, matrix.row_ptr[begin], matrix.row_ptr[end]));
+    if (row_word) {
+      const int last = end - 1;
+      const int64_t last_words = ((int64_t)(matrix.row_ptr[last + 1] - matrix.row_ptr[last]) * row_width[last] + 31) / 32;
+      plan.tile_words.push_back(make_int2(row_word[begin], (int)(row_word[last] + last_words)));
+    }
+    begin = -1;
+    count = 0;
+    nnz = 0;
+  };
+  for (int row = 0; row < matrix.rows; ++row) {
+    const int length = matrix.row_ptr[row + 1] - matrix.row_ptr[row];
+    if (length > tile_nnz) {
+      close(row);
+      plan.long_rows.push_back(row);
+      continue;
+    }
+    if (begin >= 0 && (nnz + length > tile_nnz || count + 1 > tile_rows)) close(row);
+    if (begin < 0) begin = row;
+    ++count;
+    nnz += length;
+    ++plan.short_rows;
+    plan.short_nnz += length;
+  }
+  close(matrix.rows);
+  return plan;
+}
+
+// Physical threads per row: about four nonzeros per thread in an average staged row, at least T/16.
+int choose_physical_tpr(int tpr, double mean_length) {
+  int physical = 1;
+  while (physical * 2 <= tpr && physical * 2 * 4 <= mean_length) physical *= 2;
+  while (tpr / physical > 16) physical *= 2;
+  return physical;
+}
+
+}  // namespace spmvb200
+
+struct spmv_operator {
+  int device = 0;
+  int layout = 0, dtype = 0, tpr = 0, physical_tpr = 0, tile_nnz = 0, tile_rows = 0;
+  int rows = 0, cols = 0;
+  int64_t nnz = 0;
+  spmv_memory memory{};
+  int* row_ptr = nullptr;
+  void* values = nullptr;
+  void* columns = nullptr;
+  int* row_base = nullptr;
+  int* row_word = nullptr;
+  uint8_t* row_width = nullptr;
+  uint32_t* words = nullptr;
+  int4* tiles = nullptr;
+  int2* tile_words = nullptr;
+  int* long_rows = nullptr;
+  unsigned* status = nullptr;
+  int64_t tile_count = 0;
+  int64_t long_count = 0;
+  int64_t device_bytes = 0;
+
+  ~spmv_operator() {
+    int previous = -1;
+    cudaGetDevice(&previous);
+    if (previous != device) cudaSetDevice(device);
+    for (void* pointer : {(void*)row_ptr, values, columns, (void*)row_base, (void*)row_word, (void*)row_width,
+                          (void*)words, (void*)tiles, (void*)tile_words, (void*)long_rows, (void*)status})
+      if (pointer) cudaFree(pointer);
+    if (previous >= 0 && previous != device) cudaSetDevice(previous);
+  }
+};
+
+using namespace spmvb200;
+
+namespace {
+
+KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
+  KernelArgs a{};
+  a.rows = op->rows;
+  a.row_ptr = op->row_ptr;
+  a.columns = op->columns;
+  a.row_base = op->row_base;
+  a.row_word = op->row_word;
+  a.row_width = op->row_width;
+  a.words = op->words;
+  a.values = op->values;
+  a.x = x;
+  a.y = y;
+  a.tiles = op->tiles;
+  a.tile_words = op->tile_words;
+  a.tile_count = op->tile_count;
+  a.tile_nnz = op->tile_nnz;
+  a.tile_rows = op->tile_rows;
+  a.row_list = op->long_rows;
+  a.row_count = op->long_count;
+  a.vector_blocks = op->long_count > 0 ? (op->long_count * op->tpr + kTileBlock - 1) / kTileBlock : 0;
+  a.status = op->status;
+  return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+void spmv_operator_config_init(spmv_operator_config* config, int layout, int dtype, int tpr) {
+  if (!config) return;
+  std::memset(config, 0, sizeof(*config));
+  config->layout = layout;
+  config->dtype = dtype;
+  config->tpr = tpr;
+  config->device = -1;
+}
+
+int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* config, spmv_operator** out) {
+  return guarded([&] {
+    require(matrix && config && out, "matrix, config and out are required");
+    *out = nullptr;
+    const Csr& m = matrix->m;
+    const int layout = config->layout, dtype = config->dtype, tpr = config->tpr;
+    const int value_bytes = value_bytes_of(dtype);
+    column_bytes_of(layout);
+    require(valid_tpr(tpr), "threads per row must be 2, 4, 8, 16 or 32");
+    require(config->physical_tpr == 0 || tile_variant_exists(tpr, config->physical_tpr),
+            "physical_tpr must divide T with T / physical_tpr in {1, 2, 4, 8, 16}");
+    require(config->tile_nnz == 0 || (config->tile_nnz >= 64 && config->tile_nnz <= 16384),
+            "tile_nnz must be 0 or in [64, 16384]");
+    int device_count = 0;
+    if (cudaGetDeviceCount(&device_count) != cudaSuccess || device_count == 0)
+      fail(SPMV_ERR_UNSUPPORTED, "no CUDA device");
+    DeviceScope scope(config->device);
+
+    // admissibility and byte model need the widest span, and the lp word count at this T
+    Facts facts;
+    for (int row = 0; row < m.rows; ++row)
+      if (m.row_ptr[row + 1] > m.row_ptr[row])
+        facts.widest_row_span = std::max(facts.widest_row_span, m.col_ind[m.row_ptr[row + 1] - 1] - m.col_ind[m.row_ptr[row]]);
+    if (layout == SPMV_LAYOUT_LP) facts.lane_packed_words[tpr_slot(tpr)] = lane_packed_word_count(m, tpr);
+    if (!admissible(m, facts, layout, tpr))
+      fail(SPMV_ERR_NOT_ADMISSIBLE, "layout not admissible for this matrix");
+
+    std::unique_ptr<spmv_operator> op(new spmv_operator);
+    cuda_check(cudaGetDevice(&op->device), "cudaGetDevice");
+    op->layout = layout;
+    op->dtype = dtype;
+    op->tpr = tpr;
+    op->rows = m.rows;
+    op->cols = m.cols;
+    op->nnz = m.nnz();
+    op->memory = memory_of(m, facts, layout, dtype, tpr);
+    op->tile_nnz = config->tile_nnz > 0 ? config->tile_nnz : 2048;
+    op->tile_rows = std::max(64, op->tile_nnz / 2);
+    {
+      int shared_limit = 0;
+      cuda_check(cudaDeviceGetAttribute(&shared_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, op->device), "device attribute");
+      const TileSmem smem = tile_smem(op->tile_nnz, op->tile_rows, value_bytes, layout);
+      if (smem.total > shared_limit)
+        fail(SPMV_ERR_INVALID_ARGUMENT, "tile_nnz needs " + std::to_string(smem.total) + " bytes of shared memory, above the " +
+                                            std::to_string(shared_limit) + " a block may have");
+    }
+
+    // encoded streams
+    const size_t nnz = (size_t)m.nnz();
+    op->row_ptr = device_upload<int>(m.row_ptr.data(), (size_t)m.rows + 1, op->device_bytes);
+    {
+      std::vector<unsigned char> converted(nnz * value_bytes);
+      convert_values(dtype, m.val.data(), (int64_t)nnz, config->value_rounding, converted.data());
+      op->values = device_upload<unsigned char>(converted.data(), converted.size(), op->device_bytes);
+    }
+    std::vector<int> row_word;
+    std::vector<uint8_t> row_width;
+    switch (layout) {
+      case SPMV_LAYOUT_I32:
+        op->columns = device_upload<int>(m.col_ind.data(), nnz, op->device_bytes);
+        break;
+      case SPMV_LAYOUT_I16: case SPMV_LAYOUT_I8: {
+        std::vector<unsigned char> narrow(nnz * column_bytes_of(layout));
+        encode_absolute(m, column_bytes_of(layout), narrow.data());
+        op->columns = device_upload<unsigned char>(narrow.data(), narrow.size(), op->device_bytes);
+        break;
+      }
+      case SPMV_LAYOUT_R16: case SPMV_LAYOUT_R8: {
+        std::vector<unsigned char> offsets(nnz * column_bytes_of(layout));
+        encode_relative(m, column_bytes_of(layout), offsets.data());
+        op->columns = device_upload<unsigned char>(offsets.data(), offsets.size(), op->device_bytes);
+        break;
+      }
+      default: {
+        const int64_t word_count = facts.lane_packed_words[tpr_slot(tpr)];
+        std::vector<uint32_t> words((size_t)word_count);
+        row_word.resize((size_t)m.rows);
+        row_width.resize((size_t)m.rows);
+        encode_lane_packed(m, tpr, word_count, row_word.data(), row_width.data(), words.data());
+        op->words = device_upload<uint32_t>(words.data(), words.size(), op->device_bytes);
+        op->row_word = device_upload<int>(row_word.data(), row_word.size(), op->device_bytes);
+        op->row_width = device_upload<uint8_t>(row_width.data(), row_width.size(), op->device_bytes);
+        break;
+      }
+    }
+    if (layout == SPMV_LAYOUT_R16 || layout == SPMV_LAYOUT_R8 || layout == SPMV_LAYOUT_LP) {
+      std::vector<int> bases((size_t)m.rows);
+      encode_row_base(m, bases.data());
+      op->row_base = device_upload<int>(bases.data(), bases.size(), op->device_bytes);
+    }
+
+    // tile plan
+    const TilePlan plan = plan_tiles(m, op->tile_nnz, op->tile_rows, layout == SPMV_LAYOUT_LP ? row_word.data() : nullptr,
+                                     layout == SPMV_LAYOUT_LP ? row_width.data() : nullptr);
+    op->tile_count = (int64_t)plan.tiles.size();
+    op->long_count = (int64_t)plan.long_rows.size();
+    op->tiles = device_upload<int4>(plan.tiles.data(), plan.tiles.size(), op->device_bytes);
+    if (layout == SPMV_LAYOUT_LP)
+      op->tile_words = device_upload<int2>(plan.tile_words.data(), plan.tile_words.size(), op->device_bytes);
+    op->long_rows = device_upload<int>(plan.long_rows.data(), plan.long_rows.size(), op->device_bytes);
+    op->status = device_upload<unsigned>(nullptr, 1, op->device_bytes);
+    cuda_check(cudaMemset(op->status, 0, sizeof(unsigned)), "cudaMemset");
+    const double mean = plan.short_rows > 0 ? (double)plan.short_nnz / (double)plan.short_rows : 0.0;
+    op->physical_tpr = config->physical_tpr > 0 ? config->physical_tpr : choose_physical_tpr(tpr, mean);
+    if (op->tile_count + (op->long_count * tpr + kTileBlock - 1) / kTileBlock > 0x7fffffff)
+      fail(SPMV_ERR_TOO_LARGE, "grid exceeds 2^31-1 blocks");
+    cuda_check(cudaDeviceSynchronize(), "operator upload");
+    *out = op.release();
+  });
+}
+
+int spmv_operator_get_info(const spmv_operator* op, spmv_operator_info* info) {
+  return guarded([&] {
+    require(op && info, "op and info are required");
+    info->rows = op->rows;
+    info->cols = op->cols;
+    info->nnz = op->nnz;
+    info->layout = op->layout;
+    info->dtype = op->dtype;
+    info->tpr = op->tpr;
+    info->physical_tpr = op->physical_tpr;
+    info->tile_nnz = op->tile_nnz;
+    info->tiles = op->tile_count;
+    info->long_rows = op->long_count;
+    info->device_bytes = op->device_bytes;
+    info->memory = op->memory;
+  });
+}
+
+int spmv_operator_run(const spmv_operator* op, const void* x, void* y, void* stream) {
+  return guarded([&] {
+    require(op && x && y, "op, x and y are required");
+    const KernelArgs a = kernel_args(op, x, y);
+    cuda_check(launch_tiles(op->dtype, op->layout, op->tpr, op->physical_tpr, a, static_cast<cudaStream_t>(stream)),
+               "SpMV launch");
+  });
+}
+
+int spmv_operator_run_host(const spmv_operator* op, const void* x_host, void* y_host, void* x_device, void* y_device,
+                           void* stream) {
+  return guarded([&] {
+    require(op && x_host && y_host && x_device && y_device, "all buffers are required");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t value_bytes = (size_t)value_bytes_of(op->dtype);
+    cuda_check(cudaMemcpyAsync(x_device, x_host, value_bytes * op->cols, cudaMemcpyHostToDevice, s), "copy x");
+    const KernelArgs a = kernel_args(op, x_device, y_device);
+    cuda_check(launch_tiles(op->dtype, op->layout, op->tpr, op->physical_tpr, a, s), "SpMV launch");
+    cuda_check(cudaMemcpyAsync(y_host, y_device, value_bytes * op->rows, cudaMemcpyDeviceToHost, s), "copy y");
+    cuda_check(cudaStreamSynchronize(s), "stream synchronize");
+  });
+}
+
+int spmv_operator_check(const spmv_operator* op) {
+  int timed_out = 0;
+  const int status = guarded([&] {
+    require(op, "op is required");
+    DeviceScope scope(op->device);
+    cuda_check(cudaDeviceSynchronize(), "device synchronize");
+    unsigned word = 0;
+    cuda_check(cudaMemcpy(&word, op->status, sizeof(word), cudaMemcpyDeviceToHost), "read status");
+    cuda_check(cudaMemset(op->status, 0, sizeof(unsigned)), "clear status");
+    if (word & kStatusTimeout) {
+      timed_out = 1;
+      set_last_error("a bounded device-side wait gave up");
+    } else if (word & kStatusAlignment) {
+      set_last_error("a bulk copy was not 16-byte aligned and was replaced by plain loads");
+    }
+  });
+  return status != SPMV_OK ? status : (timed_out ? SPMV_ERR_TIMEOUT : SPMV_OK);
+}
+
+int spmv_operator_get_arrays(const spmv_operator* op, spmv_operator_arrays* arrays) {
+  return guarded([&] {
+    require(op && arrays, "op and arrays are required");
+    arrays->row_ptr = op->row_ptr;
+    arrays->columns = op->columns;
+    arrays->row_base = op->row_base;
+    arrays->row_word = op->row_word;
+    arrays->row_width = op->row_width;
+    arrays->words = op->words;
+    arrays->values = op->values;
+  });
+}
+
+void spmv_operator_destroy(spmv_operator* op) { delete op; }
+
+int spmv_launch(int layout, int dtype, int tpr, const spmv_device_matrix* matrix, void* stream) {
+  return guarded([&] {
+    require(matrix, "matrix is required");
+    value_bytes_of(dtype);
+    column_bytes_of(layout);
+    require(valid_tpr(tpr), "threads per row must be 2, 4, 8, 16 or 32");
+    require(matrix->rows >= 0 && matrix->row_ptr && matrix->values && matrix->x && matrix->y, "missing arrays");
+    if (layout == SPMV_LAYOUT_LP) require(matrix->row_base && matrix->row_word && matrix->row_width && matrix->words, "missing lp arrays");
+    else require(matrix->columns != nullptr, "missing columns");
+    if (layout == SPMV_LAYOUT_R16 || layout == SPMV_LAYOUT_R8) require(matrix->row_base != nullptr, "missing row_base");
+    KernelArgs a{};
+    a.rows = matrix->rows;
+    a.row_ptr = matrix->row_ptr;
+    a.columns = matrix->columns;
+    a.row_base = matrix->row_base;
+    a.row_word = matrix->row_word;
+    a.row_width = matrix->row_width;
+    a.words = matrix->words;
+    a.values = matrix->values;
+    a.x = matrix->x;
+    a.y = matrix->y;
+    a.row_list = nullptr;
+    a.row_count = matrix->rows;
+    // one vector of T threads per row, as the reference launches (bench_csr_width.cu:525-526)
+    const int64_t blocks = ((int64_t)matrix->rows * tpr + kVectorBlock - 1) / kVectorBlock;
+    require(blocks <= 0x7fffffff, "too many rows for one launch");
+    cuda_check(launch_vector(dtype, layout, tpr, a, blocks, static_cast<cudaStream_t>(stream)), "SpMV launch");
+  });
+}
+
+}  // extern "C"

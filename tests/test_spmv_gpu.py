@@ -1,0 +1,229 @@
+"""GPU parity: the library's sm_100a kernels against the CPU oracle (bit for bit), against the reference's own
+kernels rebuilt for sm_100a (bit for bit), and against cuSPARSE (within the north-star tolerance). Every
+product goes through the C ABI (spmv_operator_run / spmv_launch)."""
+import numpy as np
+import pytest
+
+import oracle
+import spmvb200 as spmv
+from conftest import random_csr
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+LAYOUTS = (spmv.I32, spmv.I16, spmv.R16, spmv.LP, spmv.I8, spmv.R8)
+DTYPES = (spmv.F64, spmv.F32, spmv.F16)
+TORCH = {spmv.F64: torch.float64, spmv.F32: torch.float32, spmv.F16: torch.float16}
+
+
+def bits(array):
+    return np.ascontiguousarray(array).view(np.uint8)
+
+
+def device_run(op, x, stream=0):
+    x_device = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    y_device = torch.full((op.rows,), float("nan"), dtype=TORCH[op.dtype], device="cuda")
+    op.run(x_device.data_ptr(), y_device.data_ptr(), stream)
+    torch.cuda.synchronize()
+    op.check()
+    return y_device.cpu().numpy()
+
+
+def oracle_product(matrix, x, dtype, layout, tpr):
+    row_ptr, col_ind, values = matrix.arrays()
+    return oracle.spmv_csr(row_ptr, col_ind, values, x, dtype, layout, tpr)
+
+
+def admissible(matrix, layout, tpr):
+    return spmv.configuration_admissible(matrix, None, spmv.Configuration.of(layout, spmv.F64, tpr))
+
+
+def physical_variants(tpr):
+    return [tpr // slots for slots in (1, 2, 4, 8, 16) if tpr // slots >= 1 and tpr % slots == 0]
+
+
+@pytest.fixture(scope="module")
+def ragged():
+    """Ragged rows: empty rows, rows of 1..60, a few rows longer than any tile (2048 default)."""
+    rows, cols = 3000, 2500
+    row_ptr, col_ind, values = random_csr(rows, cols, lambda rng: rng.integers(0, 60), 7, empty_every=23,
+                                          long_rows={11: 2400, 1500: 2049, 2999: 2500})
+    return spmv.CsrMatrix.from_arrays(rows, cols, row_ptr, col_ind, values, name="ragged")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("tpr", spmv.THREADS_PER_ROW)
+def test_operator_matches_oracle_every_layout(ragged, dtype, tpr):
+    x = spmv.fill_uniform(dtype, ragged.cols, 11)
+    for layout in (spmv.I32, spmv.I16, spmv.R16, spmv.LP):
+        if not admissible(ragged, layout, tpr):
+            continue
+        expected = oracle_product(ragged, x, dtype, layout, tpr)
+        with spmv.Operator(ragged, layout, dtype, tpr) as op:
+            assert op.info().long_rows == 3
+            y = device_run(op, x)
+        assert np.array_equal(bits(y), bits(expected)), (spmv.LAYOUT_NAMES[layout], tpr)
+
+
+@pytest.mark.parametrize("tpr", spmv.THREADS_PER_ROW)
+def test_every_physical_mapping_and_tile_size(ragged, tpr):
+    """The result must not depend on how many threads run a row nor on the tile size."""
+    dtype = spmv.F32
+    x = spmv.fill_uniform(dtype, ragged.cols, 5)
+    for layout in (spmv.I32, spmv.R16, spmv.LP):
+        expected = oracle_product(ragged, x, dtype, layout, tpr)
+        for physical in physical_variants(tpr):
+            for tile_nnz in (64, 700, 2048, 8192):
+                with spmv.Operator(ragged, layout, dtype, tpr, physical_tpr=physical, tile_nnz=tile_nnz) as op:
+                    y = device_run(op, x)
+                assert np.array_equal(bits(y), bits(expected)), (spmv.LAYOUT_NAMES[layout], tpr, physical, tile_nnz)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_narrow_8bit_layouts(dtype):
+    rows, cols = 700, 256
+    row_ptr, col_ind, values = random_csr(rows, cols, 20, 3, empty_every=9, long_rows={4: 256})
+    matrix = spmv.CsrMatrix.from_arrays(rows, cols, row_ptr, col_ind, values)
+    x = spmv.fill_uniform(dtype, cols, 2)
+    for tpr in spmv.THREADS_PER_ROW:
+        for layout in (spmv.I8, spmv.R8):
+            assert admissible(matrix, layout, tpr)
+            with spmv.Operator(matrix, layout, dtype, tpr, tile_nnz=128) as op:
+                y = device_run(op, x)
+            assert np.array_equal(bits(y), bits(oracle_product(matrix, x, dtype, spmv.I32, tpr)))
+
+
+def test_inadmissible_layouts_are_refused():
+    matrix = spmv.synth_random_band(70000, 2000, 8.0, 1)      # n > 2^16: i16 not admissible
+    with pytest.raises(spmv.SpmvError) as failure:
+        spmv.Operator(matrix, spmv.I16, spmv.F32, 8)
+    assert failure.value.status == spmv.ERR_NOT_ADMISSIBLE
+    wide = spmv.CsrMatrix.from_arrays(2, 100000, [0, 2, 3], [0, 99999, 5])
+    with pytest.raises(spmv.SpmvError) as failure:
+        spmv.Operator(wide, spmv.R16, spmv.F32, 8)
+    assert failure.value.status == spmv.ERR_NOT_ADMISSIBLE
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_degenerate_matrices(dtype):
+    cases = [
+        spmv.CsrMatrix.from_arrays(5, 7, [0, 0, 0, 0, 0, 0], []),                       # no nonzeros
+        spmv.CsrMatrix.from_arrays(1, 1, [0, 1], [0], [2.5]),                           # 1 x 1
+        spmv.CsrMatrix.from_arrays(3, 40000, [0, 0, 40000, 40000], np.arange(40000)),    # one row wider than tiles
+        spmv.CsrMatrix.from_arrays(4, 3, [0, 1, 2, 3, 3], [2, 1, 0], [-0.0, 1.0, -1.0]),  # -0 product, rectangular
+    ]
+    for matrix in cases:
+        x = spmv.fill_uniform(dtype, matrix.cols, 9)
+        for tpr in (2, 32):
+            for layout in (spmv.I32, spmv.LP):
+                with spmv.Operator(matrix, layout, dtype, tpr) as op:
+                    y = device_run(op, x)
+                assert np.array_equal(bits(y), bits(oracle_product(matrix, x, dtype, layout, tpr)))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("tpr", spmv.THREADS_PER_ROW)
+def test_raw_launch_matches_oracle(ragged, dtype, tpr):
+    """spmv_launch over caller-owned device arrays (the launch<T> shape, no preprocessing)."""
+    row_ptr, col_ind, values = ragged.arrays()
+    x = spmv.fill_uniform(dtype, ragged.cols, 4)
+    typed = oracle.convert_values(values, dtype)
+    for layout in (spmv.I32, spmv.I16, spmv.R16, spmv.LP):
+        if not admissible(ragged, layout, tpr):
+            continue
+        streams = oracle.encode(row_ptr, col_ind, layout, tpr)
+        dev = {key: torch.from_numpy(np.ascontiguousarray(value)).cuda() for key, value in streams.items()}
+        d_row_ptr = torch.from_numpy(row_ptr).cuda()
+        d_values = torch.from_numpy(typed).cuda()
+        d_x = torch.from_numpy(x).cuda()
+        d_y = torch.zeros(ragged.rows, dtype=TORCH[dtype], device="cuda")
+        matrix = spmv.DeviceMatrix(ragged.rows, ragged.cols, col_ind.size, d_row_ptr.data_ptr(),
+                                   dev["columns"].data_ptr() if "columns" in dev else None,
+                                   dev["row_base"].data_ptr() if "row_base" in dev else None,
+                                   dev["row_word"].data_ptr() if "row_word" in dev else None,
+                                   dev["row_width"].data_ptr() if "row_width" in dev else None,
+                                   dev["words"].data_ptr() if "words" in dev else None,
+                                   d_values.data_ptr(), d_x.data_ptr(), d_y.data_ptr())
+        spmv.launch(layout, dtype, tpr, matrix)
+        torch.cuda.synchronize()
+        expected = oracle.spmv(dtype, layout, tpr, row_ptr, typed, x, **streams)
+        assert np.array_equal(bits(d_y.cpu().numpy()), bits(expected))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_reference_kernels_agree_bit_for_bit(ragged, reference, dtype):
+    """The reference's kernels (launch<T>, bench_csr_width.cu:607) rebuilt for sm_100a on the operator's own
+    device arrays give the same bits as the library and as the oracle."""
+    x = spmv.fill_uniform(dtype, ragged.cols, 21)
+    d_x = torch.from_numpy(x).cuda()
+    for tpr in spmv.THREADS_PER_ROW:
+        for layout in (spmv.I32, spmv.I16, spmv.R16, spmv.LP):
+            if not admissible(ragged, layout, tpr):
+                continue
+            with spmv.Operator(ragged, layout, dtype, tpr) as op:
+                arrays = op.arrays()
+                d_y = torch.zeros(ragged.rows, dtype=TORCH[dtype], device="cuda")
+                status = reference.launch(dtype, layout, tpr, ragged.rows, ragged.cols, ragged.nnz, arrays.row_ptr,
+                                          arrays.columns, arrays.row_base, arrays.row_word, arrays.row_width,
+                                          arrays.words, arrays.values, d_x.data_ptr(), d_y.data_ptr())
+                assert status == 0
+                theirs = d_y.cpu().numpy()
+                mine = device_run(op, x)
+            assert np.array_equal(bits(mine), bits(theirs)), (spmv.LAYOUT_NAMES[layout], tpr)
+            assert np.array_equal(bits(mine), bits(oracle_product(ragged, x, dtype, layout, tpr)))
+
+
+def l2_relative(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300)
+
+
+# tolerances of the cuSPARSE comparison (relative, L2 norm): FP64 1e-12, FP32 1e-5, FP16 1e-2
+CUSPARSE_TOLERANCE = {spmv.F64: 1e-12, spmv.F32: 1e-5, spmv.F16: 1e-2}
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_cusparse_agrees_within_tolerance(ragged, dtype):
+    """torch's CSR product (cuSPARSE) on the same values; FP16 computed in FP32 as the reference does (:1066)."""
+    row_ptr, col_ind, values = ragged.arrays()
+    x = spmv.fill_uniform(dtype, ragged.cols, 8)
+    compute = torch.float32 if dtype == spmv.F16 else TORCH[dtype]
+    typed = torch.from_numpy(oracle.convert_values(values, dtype)).to(compute)
+    a = torch.sparse_csr_tensor(torch.from_numpy(row_ptr.astype(np.int64)), torch.from_numpy(col_ind.astype(np.int64)),
+                                typed, size=(ragged.rows, ragged.cols)).cuda()
+    reference_y = (a @ torch.from_numpy(x).to(compute).cuda().unsqueeze(1)).squeeze(1).cpu().numpy()
+    with spmv.Operator(ragged, spmv.LP, dtype, 8) as op:
+        y = device_run(op, x)
+    assert l2_relative(y, reference_y) <= CUSPARSE_TOLERANCE[dtype]
+
+
+def test_streams_and_repeated_runs(ragged):
+    """Products on a side stream, repeated, with the same bits every time."""
+    x = spmv.fill_uniform(spmv.F64, ragged.cols, 1)
+    stream = torch.cuda.Stream()
+    with spmv.Operator(ragged, spmv.R16, spmv.F64, 16) as op:
+        first = device_run(op, x, stream.cuda_stream)
+        for _ in range(3):
+            assert np.array_equal(bits(device_run(op, x, stream.cuda_stream)), bits(first))
+
+
+def test_run_host_round_trip(ragged):
+    x = spmv.fill_uniform(spmv.F32, ragged.cols, 3)
+    with spmv.Operator(ragged, spmv.I32, spmv.F32, 4) as op:
+        y = np.zeros(ragged.rows, np.float32)
+        x_device = torch.empty(ragged.cols, dtype=torch.float32, device="cuda")
+        y_device = torch.empty(ragged.rows, dtype=torch.float32, device="cuda")
+        op.run_host(x, y, x_device.data_ptr(), y_device.data_ptr())
+    assert np.array_equal(bits(y), bits(oracle_product(ragged, x, spmv.F32, spmv.I32, 4)))
+
+
+def test_laplacian_config_bit_identical():
+    """The 5-point Laplacian on 256 x 256, FP64, x uniform from seed 0, CSR-i32/i16/r16 at T = 4: every
+    layout bit-identical to the CPU CSR-i32 product."""
+    matrix = spmv.synth_laplacian2d(256)
+    x = spmv.fill_uniform(spmv.F64, matrix.cols, 0)
+    expected = oracle_product(matrix, x, spmv.F64, spmv.I32, 4)
+    for layout in (spmv.I32, spmv.I16, spmv.R16):
+        with spmv.Operator(matrix, layout, spmv.F64, 4) as op:
+            assert np.array_equal(bits(device_run(op, x)), bits(expected))
