@@ -7,6 +7,7 @@
 #include "internal.hpp"
 
 #include <cerrno>
+#include <sched.h>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -16,10 +17,17 @@
 
 namespace spmvb200 {
 
+// The CPUs this process may run on (its affinity mask, which a container or job scheduler narrows),
+// or SPMV_HOST_THREADS.
 int host_threads() {
   static const int threads = [] {
     const char* forced = std::getenv("SPMV_HOST_THREADS");
-    int count = forced ? std::atoi(forced) : (int)std::thread::hardware_concurrency();
+    int count = forced ? std::atoi(forced) : 0;
+    if (count <= 0) {
+      cpu_set_t mask;
+      CPU_ZERO(&mask);
+      count = sched_getaffinity(0, sizeof(mask), &mask) == 0 ? CPU_COUNT(&mask) : (int)std::thread::hardware_concurrency();
+    }
     return std::max(1, std::min(count, 64));
   }();
   return threads;
