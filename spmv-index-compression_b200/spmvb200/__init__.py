@@ -535,9 +535,11 @@ class Operator:
         """y = A x on a CUDA stream (device pointers as integers, e.g. torch tensor.data_ptr())."""
         _check(_lib.spmv_operator_run(self._handle, x_ptr, y_ptr, stream or None))
 
-    def run_host(self, x_host: np.ndarray, y_host: np.ndarray, x_device: int, y_device: int, stream: int = 0):
-        """Copies x in, multiplies, copies y out and waits (result_at_fixed_tpr, bench_csr_width.cu:779)."""
-        _check(_lib.spmv_operator_run_host(self._handle, _pointer(x_host), _pointer(y_host), x_device, y_device,
+    def run_host(self, x_host, y_host, x_device: int, y_device: int, stream: int = 0):
+        """Copies x in, multiplies, copies y out and waits (result_at_fixed_tpr, bench_csr_width.cu:779).
+        x_host / y_host are numpy arrays or host pointers (e.g. of pinned torch tensors)."""
+        host = lambda array: array if isinstance(array, int) else _pointer(array)  # noqa: E731
+        _check(_lib.spmv_operator_run_host(self._handle, host(x_host), host(y_host), x_device, y_device,
                                            stream or None))
 
     def check(self):
