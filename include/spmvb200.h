@@ -180,9 +180,10 @@ typedef struct {
   int tile_nnz;           /* nonzeros staged per tile (0 = default)                                  */
   int value_rounding;     /* 0: values (T)(float)val as upload_matrix does (:927); 1: (T)val          */
   int device;             /* CUDA device ordinal (-1 = current device)                               */
+  int stages;             /* shared-memory tile buffers per CTA, 1..4 (0 = default)                  */
 } spmv_operator_config;
 
-/* Fills a config with defaults: physical_tpr 0, tile_nnz 0, value_rounding 0, device -1. */
+/* Fills a config with defaults: physical_tpr 0, tile_nnz 0, value_rounding 0, device -1, stages 0. */
 void spmv_operator_config_init(spmv_operator_config* config, int layout, int dtype, int tpr);
 
 /* upload_matrix + upload_* (bench_csr_width.cu:795-951): encodes the matrix in the layout, converts
@@ -200,6 +201,9 @@ typedef struct {
   int physical_tpr;
   int tile_nnz;
   int64_t tiles;             /* staged tiles of short rows                                   */
+  int64_t tile_ctas;         /* persistent CTAs over the tiles                               */
+  int stages;                /* shared-memory tile buffers per CTA                           */
+  int tile_rows;             /* rows a tile holds at most                                    */
   int64_t long_rows;         /* rows longer than a tile, streamed by the long-row path       */
   int64_t device_bytes;      /* bytes of device memory the operator holds                    */
   spmv_memory memory;        /* memory_of of this layout at this T (algorithmic bytes/product) */

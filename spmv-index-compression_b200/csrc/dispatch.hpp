@@ -14,10 +14,15 @@ inline bool tile_variant_exists(int tpr, int physical_tpr) {
   return slots == 1 || slots == 2 || slots == 4 || slots == 8 || slots == 16;
 }
 
-// k_spmv_tiles over a.vector_blocks + a.tile_count CTAs with the shared memory of the tile plan.
+// k_spmv_tiles over a.vector_blocks + a.tile_ctas CTAs with the shared memory of the tile plan.
 cudaError_t launch_tiles_f64(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream);
 cudaError_t launch_tiles_f32(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream);
 cudaError_t launch_tiles_f16(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream);
+// Resident k_spmv_tiles CTAs per multiprocessor with `smem` bytes of dynamic shared memory (0 if the
+// variant does not exist); also raises the kernel's shared-memory limit to smem.
+int tiles_occupancy_f64(int layout, int tpr, int physical_tpr, int smem);
+int tiles_occupancy_f32(int layout, int tpr, int physical_tpr, int smem);
+int tiles_occupancy_f16(int layout, int tpr, int physical_tpr, int smem);
 // k_spmv_vector over `blocks` CTAs of kVectorBlock threads.
 cudaError_t launch_vector_f64(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream);
 cudaError_t launch_vector_f32(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream);
@@ -28,6 +33,14 @@ inline cudaError_t launch_tiles(int dtype, int layout, int tpr, int physical_tpr
     case SPMV_F64: return launch_tiles_f64(layout, tpr, physical_tpr, a, stream);
     case SPMV_F32: return launch_tiles_f32(layout, tpr, physical_tpr, a, stream);
     default:       return launch_tiles_f16(layout, tpr, physical_tpr, a, stream);
+  }
+}
+
+inline int tiles_occupancy(int dtype, int layout, int tpr, int physical_tpr, int smem) {
+  switch (dtype) {
+    case SPMV_F64: return tiles_occupancy_f64(layout, tpr, physical_tpr, smem);
+    case SPMV_F32: return tiles_occupancy_f32(layout, tpr, physical_tpr, smem);
+    default:       return tiles_occupancy_f16(layout, tpr, physical_tpr, smem);
   }
 }
 

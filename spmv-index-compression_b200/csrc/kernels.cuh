@@ -7,33 +7,41 @@
 // offset o = T/2, ..., 1, s_i += s_{i+o}; lane 0 narrows s_0 into y.
 //
 // Which hardware thread runs which logical lane is free. These kernels run a row on P threads (P divides
-// T): thread p owns the logical lanes p, p+P, p+2P, ... (T/P "slots"), so it walks the entries p, p+P,
+// T): thread p owns the logical lanes p, p+P, p+2P, ... (S = T/P "slots"), so it walks the entries p, p+P,
 // p+2P, ... of the row and adds entry e into slot ((e - row_begin) mod T) / P. The tree levels with
 // o >= P pair two lanes of the same thread and run in registers; the last log2(P) levels are shuffles.
 // Lane sums start at +0.0 and an FMA chain or a sum never produces -0.0 from it, so the zero sums of
 // empty lanes are exact no-ops, as they are in the reference.
 //
 // Kernels
-//   k_spmv_tiles   one CTA per tile: a run of consecutive rows whose nonzeros fit in shared memory.
-//                  The tile's value and column (or CSR-lp word) streams are brought in by cp.async.bulk
-//                  (the 1-D TMA engine) on an mbarrier, 16-byte-aligned interior by the bulk copy and
-//                  ragged ends by plain loads; the row metadata is read with coalesced loads. The
-//                  compute phase then reads shared memory and gathers x through the read-only path.
+//   k_spmv_tiles   persistent CTAs over the tiles of the operator's plan (runs of consecutive rows whose
+//                  nonzeros fit in shared memory). Each CTA owns tiles cta, cta + ctas, ... and keeps a
+//                  ring of `stages` shared-memory buffers: thread 0 streams upcoming tiles into free
+//                  buffers with cp.async.bulk (the 1-D TMA engine), completing on the buffer's "full"
+//                  mbarrier. On a resident tile every thread gathers x at up to 32 of its entries' decoded
+//                  columns at once into registers and adds them into its lane chains, reading values and
+//                  columns from shared memory; its warp then releases the buffer on the "empty" mbarrier
+//                  and thread 0 refills it with a later tile. The operator
+//                  pads every stream by 16 bytes, so each bulk copy is the 16-byte-aligned superset of a
+//                  tile's range. Its leading `vector_blocks` CTAs run the vector path over rows longer
+//                  than a tile.
 //   k_spmv_vector  one group of T threads per row straight from global memory (the reference's
-//                  mapping): rows longer than a tile, and the raw launch over caller arrays.
+//                  mapping): the raw launch over caller arrays, which carry no plan and no padding.
 #pragma once
 
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "spmvb200.h"
 
 namespace spmvb200 {
 
-constexpr int kTileBlock = 256;          // threads of a tile CTA
-constexpr int kVectorBlock = 128;        // threads of a vector CTA
-constexpr unsigned kStatusTimeout = 1u;  // bit of the status word: a bounded wait gave up
-constexpr unsigned kStatusAlignment = 2u;  // bit: a bulk copy was not 16-byte aligned (not issued)
+constexpr int kTileBlock = 256;            // threads of a tile CTA
+constexpr int kVectorBlock = 128;          // threads of a vector CTA
+constexpr int kMaxStages = 4;              // shared-memory buffers of a tile CTA at most
+constexpr int kStreamPadding = 16;         // bytes every operator stream carries past its end
+constexpr unsigned kStatusTimeout = 1u;    // bit of the status word: a bounded wait gave up
 
 // ---- value types --------------------------------------------------------------------------------
 template <class V> struct ValueTraits;
@@ -71,6 +79,7 @@ template <> struct LayoutTraits<SPMV_LAYOUT_LP>  { using Index = uint32_t; stati
 // Arguments of every kernel (device pointers).
 struct KernelArgs {
   int rows;
+  int cols;
   const int* row_ptr;
   const void* columns;       // absolute / row-base index stream
   const int* row_base;
@@ -81,15 +90,49 @@ struct KernelArgs {
   const void* x;
   void* y;
   const int4* tiles;         // [tile_count] {row_begin, row_end, entry_begin, entry_end}
-  const int2* tile_words;    // CSR-lp: [tile_count] {word_begin, word_end} of the tile's stream
+  const int2* tile_words;    // CSR-lp: [tile_count] {first word, last word + 1} of the tile's stream
   int64_t tile_count;
   int tile_nnz;              // nonzeros a tile holds at most
   int tile_rows;             // rows a tile holds at most
+  int stages;                // shared-memory buffers of a tile CTA (1..kMaxStages)
   const int* row_list;       // rows of the vector path (nullptr: rows 0..row_count-1)
   int64_t row_count;         // entries of row_list, or rows
   int64_t vector_blocks;     // k_spmv_tiles: its first vector_blocks CTAs run the vector path on row_list
+  int64_t tile_ctas;         // k_spmv_tiles: persistent CTAs over the tiles after the vector blocks
   unsigned* status;          // device status word (may be null)
 };
+
+// ---- shared-memory plan of a tile CTA (host and device compute it alike) ----------------------------
+// [0, 64): full[kMaxStages] and empty[kMaxStages] mbarriers; then `stages` buffers, each a header (the
+// tile's rows and image origins) and 16-byte-aligned images of the tile's row_ptr, row_base, row_word and
+// row_width slices and of its value and index (or CSR-lp word) ranges. An image starts at the 16-byte
+// boundary at or below its first element, so it holds up to 16 bytes before and after the range.
+struct StagePlan {
+  int header, row_ptr, row_base, row_word, row_width, values, index, bytes;
+};
+
+__host__ __device__ inline int round16(int bytes) { return (bytes + 15) & ~15; }
+
+__host__ __device__ inline StagePlan stage_plan(int tile_nnz, int tile_rows, int value_bytes, int layout) {
+  const bool base = layout == SPMV_LAYOUT_R16 || layout == SPMV_LAYOUT_R8 || layout == SPMV_LAYOUT_LP;
+  const bool packed = layout == SPMV_LAYOUT_LP;
+  const int index_bytes = packed ? 4 : (layout == SPMV_LAYOUT_I32 ? 4 : ((layout == SPMV_LAYOUT_I16 || layout == SPMV_LAYOUT_R16) ? 2 : 1));
+  StagePlan plan;
+  int offset = 0;
+  plan.header = offset;    offset += 32;   // row_begin, rows, 5 image origins
+  plan.row_ptr = offset;   offset += round16(4 * (tile_rows + 1)) + 16;
+  plan.row_base = offset;  if (base) offset += round16(4 * tile_rows) + 16;
+  plan.row_word = offset;  if (packed) offset += round16(4 * tile_rows) + 16;
+  plan.row_width = offset; if (packed) offset += round16(tile_rows) + 16;
+  plan.values = offset;    offset += round16(value_bytes * tile_nnz) + 16;
+  plan.index = offset;     offset += packed ? round16(4 * (tile_nnz + 1)) + 16 : round16(index_bytes * tile_nnz) + 16;
+  plan.bytes = offset;
+  return plan;
+}
+
+__host__ __device__ inline int tile_smem_bytes(int tile_nnz, int tile_rows, int value_bytes, int layout, int stages) {
+  return 64 + stages * stage_plan(tile_nnz, tile_rows, value_bytes, layout).bytes;
+}
 
 // ---- small device helpers -----------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_address(const void* pointer) {
@@ -98,11 +141,18 @@ __device__ __forceinline__ uint32_t smem_address(const void* pointer) {
 
 __device__ __forceinline__ void mbarrier_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbarrier_init_fence() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
 __device__ __forceinline__ void mbarrier_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbarrier_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ bool mbarrier_try_wait(uint32_t bar, uint32_t parity) {
@@ -123,7 +173,8 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return now;
 }
 
-// Waits for phase `parity` of an mbarrier for at most ~limit_ns. Returns false when it gave up.
+// Waits for phase `parity` of an mbarrier for at most about limit_ns (and a bounded number of polls).
+// Returns false when it gave up.
 __device__ __forceinline__ bool mbarrier_wait_bounded(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   if (mbarrier_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
@@ -134,7 +185,7 @@ __device__ __forceinline__ bool mbarrier_wait_bounded(uint32_t bar, uint32_t par
   return false;
 }
 
-// 1-D bulk copy global -> shared (TMA), completing on the mbarrier with the byte count.
+// 1-D bulk copy global -> shared (TMA), completing on the mbarrier with its byte count.
 __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
@@ -147,104 +198,27 @@ __device__ __forceinline__ T load_readonly(const T* pointer) {
   return __ldg(pointer);
 }
 template <>
-__device__ __forceinline__ __half load_readonly<__half>(const __half* pointer) {
-  return __ldg(pointer);
-}
-template <>
 __device__ __forceinline__ uint8_t load_readonly<uint8_t>(const uint8_t* pointer) {
   return (uint8_t)__ldg(reinterpret_cast<const unsigned char*>(pointer));
 }
 
-// The shared-memory image of a global range [first, last) of elements of type E: it starts at the
-// 16-byte boundary at or below element `first`, so element e sits at byte (addr(e) - start) of the
-// image. The 16-byte-aligned interior goes through one bulk copy; the head and tail (fewer than 16
-// bytes each) are loaded by the threads. Returns the bulk bytes issued by thread 0.
+// The 16-byte-aligned superset of elements [first, last) of a padded stream: its global start, bytes, and
+// the element index sitting at image byte 0.
 template <class E>
-struct StagedRange {
-  const E* origin;      // global address of image byte 0 (16-byte aligned, may precede `first`)
-  int64_t first;        // first element staged
-  int64_t last;         // one past the last element staged
-
-  __device__ __forceinline__ StagedRange(const E* base, int64_t first_, int64_t last_) : first(first_), last(last_) {
-    const uintptr_t address = reinterpret_cast<uintptr_t>(base + first_);
-    origin = reinterpret_cast<const E*>(address & ~(uintptr_t)15);
-  }
-  // element index -> position in the shared image (in elements)
-  __device__ __forceinline__ int position(int64_t element, const E* base) const {
-    return (int)(base + element - origin);
-  }
-  // bytes of the aligned interior [interior_begin, interior_end)
-  __device__ __forceinline__ void interior(const E* base, uintptr_t& begin, uintptr_t& end) const {
+struct AlignedRange {
+  uintptr_t begin;
+  uint32_t bytes;
+  int64_t origin;
+  __device__ __forceinline__ AlignedRange(const E* base, int64_t first, int64_t last) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(base + first);
     const uintptr_t b = reinterpret_cast<uintptr_t>(base + last);
-    begin = (a + 15) & ~(uintptr_t)15;
-    end = b & ~(uintptr_t)15;
-    if (end < begin) end = begin;
+    begin = a & ~(uintptr_t)15;
+    bytes = (uint32_t)(((b + 15) & ~(uintptr_t)15) - begin);
+    origin = first - (int64_t)((a - begin) / sizeof(E));
   }
 };
 
-// Bytes of a range's aligned interior and whether a bulk copy of it into image is well formed (16-byte
-// aligned source, destination and size; always true by construction, checked so that a violation
-// degrades to plain loads instead of an ill-formed copy).
-template <class E>
-__device__ __forceinline__ bool interior_copyable(const StagedRange<E>& range, const E* base, const E* image,
-                                                  uint32_t& bytes) {
-  uintptr_t begin, end;
-  range.interior(base, begin, end);
-  bytes = (uint32_t)(end - begin);
-  const uint32_t dst = smem_address(reinterpret_cast<const char*>(image) + (begin - reinterpret_cast<uintptr_t>(range.origin)));
-  return (dst & 15u) == 0 && (begin & 15u) == 0 && (bytes & 15u) == 0;
-}
-
-// Issues the bulk copy of a range's interior into image (one thread).
-template <class E>
-__device__ __forceinline__ void stage_interior(const StagedRange<E>& range, const E* base, E* image, uint32_t bar) {
-  uintptr_t begin, end;
-  range.interior(base, begin, end);
-  if (end <= begin) return;
-  const uint32_t dst = smem_address(reinterpret_cast<const char*>(image) + (begin - reinterpret_cast<uintptr_t>(range.origin)));
-  bulk_copy_g2s(dst, reinterpret_cast<const void*>(begin), (uint32_t)(end - begin), bar);
-}
-
-// Loads the elements of a range outside its bulk interior (head and tail) with plain loads; also used
-// for the whole range when the bulk copy was not issued (returns after loading everything then).
-template <class E>
-__device__ __forceinline__ void stage_edges(const StagedRange<E>& range, const E* base, E* image, bool whole) {
-  uintptr_t begin, end;
-  range.interior(base, begin, end);
-  const int64_t interior_first = whole ? range.last : (int64_t)((const E*)begin - base);
-  const int64_t interior_last = whole ? range.last : (int64_t)((const E*)end - base);
-  for (int64_t element = range.first + threadIdx.x; element < range.last; element += blockDim.x) {
-    if (!whole && element >= interior_first && element < interior_last) continue;
-    image[range.position(element, base)] = load_readonly(base + element);
-  }
-}
-
-// ---- shared-memory plan of a tile CTA (host and device compute it alike) ----------------------------
-struct TileSmem {
-  int row_ptr, row_base, row_word, row_width, values, index, total;
-};
-
-__host__ __device__ inline int round16(int bytes) { return (bytes + 15) & ~15; }
-
-__host__ __device__ inline TileSmem tile_smem(int tile_nnz, int tile_rows, int value_bytes, int layout) {
-  const bool base = layout == SPMV_LAYOUT_R16 || layout == SPMV_LAYOUT_R8 || layout == SPMV_LAYOUT_LP;
-  const bool packed = layout == SPMV_LAYOUT_LP;
-  const int index_bytes = packed ? 4 : (layout == SPMV_LAYOUT_I32 ? 4 : ((layout == SPMV_LAYOUT_I16 || layout == SPMV_LAYOUT_R16) ? 2 : 1));
-  TileSmem plan;
-  int offset = 16;                                     // [0, 8): the mbarrier
-  plan.row_ptr = offset;   offset = round16(offset + 4 * (tile_rows + 1));
-  plan.row_base = offset;  if (base) offset = round16(offset + 4 * tile_rows);
-  plan.row_word = offset;  if (packed) offset = round16(offset + 4 * tile_rows);
-  plan.row_width = offset; if (packed) offset = round16(offset + tile_rows);
-  plan.values = offset;    offset = round16(offset + value_bytes * (tile_nnz + 16 / value_bytes));
-  plan.index = offset;
-  offset = packed ? round16(offset + 4 * (tile_nnz + 8)) : round16(offset + index_bytes * (tile_nnz + 16 / index_bytes));
-  plan.total = offset;
-  return plan;
-}
-
-// ---- the reduction over the T logical lanes ----------------------------------------------------------
+// ---- the reduction over the T logical lanes -----------------------------------------------------------
 // acc[j] holds logical lane p + j*P. Levels with offset >= P add two slots of this thread; the last
 // log2(P) levels add across the P threads of the row (segments of width P within the warp).
 template <class VT, class Acc, int T, int P>
@@ -298,7 +272,7 @@ __device__ __forceinline__ void vector_rows(const KernelArgs& a, int64_t block, 
         const int width = a.row_width[row];
         const uint64_t mask = width == 0 ? 0ull : (~0ull >> (64 - width));
         const int64_t start_bit = (int64_t)width * ((int64_t)lane * quotient + (lane < remainder ? lane : remainder));
-        int64_t word = (int64_t)a.row_word[row] + (start_bit >> 5);
+        const int64_t word = (int64_t)a.row_word[row] + (start_bit >> 5);
         uint64_t window = (((uint64_t)load_readonly(a.words + word + 1) << 32) | load_readonly(a.words + word)) >> (start_bit & 31);
         int available = 64 - (int)(start_bit & 31);
         int64_t next_word = word + 2;
@@ -324,138 +298,243 @@ __device__ __forceinline__ void vector_rows(const KernelArgs& a, int64_t block, 
   }
 }
 
-// ---- k_spmv_tiles --------------------------------------------------------------------------------------
+// ---- a resident tile, from one shared-memory buffer -------------------------------------------------
+// Rows go to groups of P threads in passes; every thread runs every pass, so the shuffles of the
+// reduction always see the full warp. A thread gathers x for up to kGathers of its entries at once (R
+// rounds of its S lanes) into registers, then adds them into its lane chains in order, reading the values
+// from shared memory; a row of up to R*T entries costs one round trip to memory.
+#ifndef SPMV_TILE_GATHERS
+#define SPMV_TILE_GATHERS 32
+#endif
+constexpr int kGathers = SPMV_TILE_GATHERS;
+
+// The stage's images, shifted so that they are indexed by absolute row, entry or word.
+template <class V, int LAYOUT>
+struct TileView {
+  using Index = typename LayoutTraits<LAYOUT>::Index;
+  int row_begin, rows;
+  const int* row_ptr;
+  const int* row_base;
+  const int* row_word;
+  const uint8_t* row_width;
+  const V* values;
+  const Index* index;
+  __device__ __forceinline__ TileView(const unsigned char* stage, const StagePlan& plan) {
+    const int* header = reinterpret_cast<const int*>(stage + plan.header);
+    row_begin = header[0];
+    rows = header[1];
+    row_ptr = reinterpret_cast<const int*>(stage + plan.row_ptr) - header[2];
+    row_base = reinterpret_cast<const int*>(stage + plan.row_base) - header[3];
+    row_word = reinterpret_cast<const int*>(stage + plan.row_word) - header[3];
+    row_width = reinterpret_cast<const uint8_t*>(stage + plan.row_width) - header[4];
+    values = reinterpret_cast<const V*>(stage + plan.values) - header[5];
+    index = reinterpret_cast<const Index*>(stage + plan.index) - header[6];
+  }
+};
+
+// Delta k of a CSR-lp lane whose run starts at bit `start` of the row's stream (bit width * (lane *
+// quotient + min(lane, remainder)), lane_major_bit of the reference): bits [start + k*width, +width) of
+// the tile's words, which the two 32-bit words around it always hold (a width never exceeds 32 bits).
+__device__ __forceinline__ uint32_t packed_delta(const uint32_t* words, uint32_t bit, uint32_t mask) {
+  return __funnelshift_r(words[bit >> 5], words[(bit >> 5) + 1], bit & 31) & mask;
+}
+
 template <class V, int LAYOUT, int T, int P>
-__global__ void __launch_bounds__(kTileBlock) k_spmv_tiles(const KernelArgs a) {
+__device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned char* stage, const StagePlan& plan) {
   using VT = ValueTraits<V>;
   using Acc = typename VT::Acc;
-  using Index = typename LayoutTraits<LAYOUT>::Index;
   constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
   constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
   constexpr int S = T / P;
-  static_assert(T % P == 0 && P >= 1 && P <= 32, "P must divide T");
-
-  extern __shared__ __align__(128) unsigned char smem[];
-  const TileSmem plan = tile_smem(a.tile_nnz, a.tile_rows, (int)sizeof(V), LAYOUT);
-  int* s_row_ptr = reinterpret_cast<int*>(smem + plan.row_ptr);
-  int* s_row_base = reinterpret_cast<int*>(smem + plan.row_base);
-  int* s_row_word = reinterpret_cast<int*>(smem + plan.row_word);
-  uint8_t* s_row_width = reinterpret_cast<uint8_t*>(smem + plan.row_width);
-  V* s_values = reinterpret_cast<V*>(smem + plan.values);
-  Index* s_index = reinterpret_cast<Index*>(smem + plan.index);
-  const uint32_t bar = smem_address(smem);
-
-  if ((int64_t)blockIdx.x < a.vector_blocks) {   // rows longer than a tile, scheduled first
-    vector_rows<V, LAYOUT, T, kTileBlock>(a, blockIdx.x, a.vector_blocks);
-    return;
-  }
-  const int64_t tile_id = (int64_t)blockIdx.x - a.vector_blocks;
-  const int4 tile = a.tiles[tile_id];
-  const int row_begin = tile.x, rows = tile.y - tile.x;
-  const V* values = static_cast<const V*>(a.values);
-  const Index* index = kPacked ? reinterpret_cast<const Index*>(a.words) : static_cast<const Index*>(a.columns);
-  const StagedRange<V> value_range(values, tile.z, tile.w);
-  int64_t index_first = tile.z, index_last = tile.w;
-  if (kPacked) {
-    const int2 words = a.tile_words[tile_id];
-    index_first = words.x;
-    index_last = (int64_t)words.y + 1;   // the extraction of a row's last delta may read one word further
-  }
-  const StagedRange<Index> index_range(index, index_first, index_last);
-
-  uint32_t value_bytes = 0, index_bytes = 0;
-  const bool bulk = interior_copyable(value_range, values, s_values, value_bytes) &&
-                    interior_copyable(index_range, index, s_index, index_bytes);
-  if (threadIdx.x == 0) mbarrier_init(bar, 1);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    if (bulk) {
-      mbarrier_arrive_expect_tx(bar, value_bytes + index_bytes);
-      stage_interior(value_range, values, s_values, bar);
-      stage_interior(index_range, index, s_index, bar);
-    } else {
-      if (a.status) atomicOr(a.status, kStatusAlignment);
-      mbarrier_arrive_expect_tx(bar, 0);
-    }
-  }
-  // ragged ends of both streams (everything, without the bulk copy) and the row metadata, plain loads
-  stage_edges(value_range, values, s_values, !bulk);
-  stage_edges(index_range, index, s_index, !bulk);
-  for (int local = threadIdx.x; local <= rows; local += kTileBlock) s_row_ptr[local] = a.row_ptr[row_begin + local];
-  if (kBase)
-    for (int local = threadIdx.x; local < rows; local += kTileBlock) s_row_base[local] = a.row_base[row_begin + local];
-  if (kPacked)
-    for (int local = threadIdx.x; local < rows; local += kTileBlock) {
-      s_row_word[local] = a.row_word[row_begin + local];
-      s_row_width[local] = a.row_width[row_begin + local];
-    }
-  const bool arrived = mbarrier_wait_bounded(bar, 0, 2000000000ull);
-  if (__syncthreads_or(!arrived)) {
-    if (threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusTimeout);
-    mbarrier_wait_bounded(bar, 0, 100000000ull);   // give copies still in flight a last bounded chance
-    return;
-  }
-
-  const int value_origin = (int)(tile.z - (int64_t)value_range.position(tile.z, values));
-  const int index_origin = (int)(index_first - (int64_t)index_range.position(index_first, index));
+  // x values gathered at once per thread: 32, or 16 for FP64 when 16 lane sums or the CSR-lp decode
+  // already hold many registers (two CTAs of 256 threads per multiprocessor leave 128 per thread)
+  constexpr int kBatch = (sizeof(V) == 8 && (S >= 16 || kPacked)) ? kGathers / 2 : kGathers;
+  constexpr int R = S >= kBatch ? 1 : kBatch / S;
+  constexpr int kGroups = kTileBlock / P;
+  const TileView<V, LAYOUT> tile(stage, plan);
   const V* x = static_cast<const V*>(a.x);
   V* y = static_cast<V*>(a.y);
-  constexpr int kGroups = kTileBlock / P;
   const int group = threadIdx.x / P, p = threadIdx.x % P;
 
-  for (int first = 0; first < rows; first += kGroups) {
+  for (int first = 0; first < tile.rows; first += kGroups) {
     const int local = first + group;
+    const int row = tile.row_begin + local;
     Acc acc[S];
 #pragma unroll
     for (int j = 0; j < S; ++j) acc[j] = Acc(0);
-    if (local < rows) {
-      const int entry_begin = s_row_ptr[local], entry_end = s_row_ptr[local + 1];
+    if (local < tile.rows) {
+      const int entry_begin = tile.row_ptr[row], entry_end = tile.row_ptr[row + 1];
       if constexpr (!kPacked) {
-        const int base = kBase ? s_row_base[local] : 0;
-        for (int entry = entry_begin + p; entry < entry_end; entry += T) {
+        const int base = kBase ? tile.row_base[row] : 0;
+        for (int entry = entry_begin + p; entry < entry_end; entry += T * R) {
+          V xv[R][S];
 #pragma unroll
-          for (int j = 0; j < S; ++j) {
-            const int e = entry + j * P;
-            if (e < entry_end) {
-              const int column = base + (int)s_index[e - index_origin];
-              acc[j] = VT::fma(VT::widen(s_values[e - value_origin]), VT::widen(load_readonly(x + column)), acc[j]);
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int j = 0; j < S; ++j) {
+              const int e = entry + r * T + j * P;
+              if (e < entry_end) xv[r][j] = load_readonly(x + base + (int)tile.index[e]);
             }
-          }
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int j = 0; j < S; ++j) {
+              const int e = entry + r * T + j * P;
+              if (e < entry_end) acc[j] = VT::fma(VT::widen(tile.values[e]), VT::widen(xv[r][j]), acc[j]);
+            }
         }
       } else {
         const int length = entry_end - entry_begin;
         const int quotient = length / T, remainder = length - quotient * T;
-        const int width = s_row_width[local];
+        const uint32_t width = tile.row_width[row];
         const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
-        const uint32_t* stream = reinterpret_cast<const uint32_t*>(s_index) + (s_row_word[local] - index_origin);
-        int column[S];
-        uint32_t bit[S];
-        int mine[S];
+        const uint32_t* words = reinterpret_cast<const uint32_t*>(tile.index) + tile.row_word[row];
+        uint32_t start[S];
+        int column[S], mine[S];
 #pragma unroll
         for (int j = 0; j < S; ++j) {
           const int lane = p + j * P;
           mine[j] = quotient + (lane < remainder ? 1 : 0);
-          bit[j] = (uint32_t)width * (uint32_t)(lane * quotient + (lane < remainder ? lane : remainder));
-          column[j] = s_row_base[local];
+          start[j] = width * (uint32_t)(lane * quotient + (lane < remainder ? lane : remainder));
+          column[j] = tile.row_base[row];
         }
         const int rounds = quotient + (remainder > 0 ? 1 : 0);
-        for (int round = 0; round < rounds; ++round) {
+        for (int round = 0; round < rounds; round += R) {
+          V xv[R][S];
 #pragma unroll
-          for (int j = 0; j < S; ++j) {
-            if (round < mine[j]) {
-              const uint32_t at = bit[j];
-              const uint32_t delta = __funnelshift_r(stream[at >> 5], stream[(at >> 5) + 1], at & 31) & mask;
-              column[j] += (int)delta;
-              bit[j] = at + (uint32_t)width;
-              const int e = entry_begin + p + j * P + round * T;
-              acc[j] = VT::fma(VT::widen(s_values[e - value_origin]), VT::widen(load_readonly(x + column[j])), acc[j]);
-            }
-          }
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int j = 0; j < S; ++j)
+              if (round + r < mine[j]) {
+                column[j] += (int)packed_delta(words, start[j] + (uint32_t)(round + r) * width, mask);
+                xv[r][j] = load_readonly(x + column[j]);
+              }
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int j = 0; j < S; ++j)
+              if (round + r < mine[j])
+                acc[j] = VT::fma(VT::widen(tile.values[entry_begin + p + j * P + (round + r) * T]), VT::widen(xv[r][j]), acc[j]);
         }
       }
     }
     const Acc sum = reduce_lanes<VT, Acc, T, P>(acc);
-    if (p == 0 && local < rows) y[row_begin + local] = VT::narrow(sum);
+    if (p == 0 && local < tile.rows) y[row] = VT::narrow(sum);
+  }
+}
+
+// Thread 0: streams tile `tile_id` into a stage and arms its full barrier with the byte count.
+template <class V, int LAYOUT>
+__device__ __forceinline__ void issue_tile(const KernelArgs& a, int64_t tile_id, unsigned char* stage, const StagePlan& plan,
+                                           uint32_t full) {
+  using Index = typename LayoutTraits<LAYOUT>::Index;
+  constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
+  constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
+  const int4 tile = a.tiles[tile_id];
+  const AlignedRange<int> row_ptr(a.row_ptr, tile.x, (int64_t)tile.y + 1);
+  const AlignedRange<int> row_base(kBase ? a.row_base : a.row_ptr, tile.x, tile.y);
+  const AlignedRange<uint8_t> row_width(kPacked ? a.row_width : reinterpret_cast<const uint8_t*>(a.row_ptr), tile.x, tile.y);
+  const AlignedRange<V> values(static_cast<const V*>(a.values), tile.z, tile.w);
+  const Index* index_base = kPacked ? reinterpret_cast<const Index*>(a.words) : static_cast<const Index*>(a.columns);
+  int64_t index_first = tile.z, index_last = tile.w;
+  if (kPacked) {
+    const int2 words = a.tile_words[tile_id];
+    index_first = words.x;
+    index_last = (int64_t)words.y + 1;    // a window reads one word past the row's last
+  }
+  const AlignedRange<Index> index(index_base, index_first, index_last);
+  int* header = reinterpret_cast<int*>(stage + plan.header);
+  header[0] = tile.x;
+  header[1] = tile.y - tile.x;
+  header[2] = (int)row_ptr.origin;
+  header[3] = (int)row_base.origin;
+  header[4] = (int)row_width.origin;
+  header[5] = (int)values.origin;
+  header[6] = (int)index.origin;
+  uint32_t bytes = row_ptr.bytes + values.bytes + index.bytes;
+  if (kBase) bytes += row_base.bytes;
+  if (kPacked) bytes += row_base.bytes + row_width.bytes;   // row_word has the extent of row_base
+  mbarrier_arrive_expect_tx(full, bytes);
+  // a range may be empty (a tile of empty rows has no values): no copy is issued for 0 bytes
+  if (row_ptr.bytes)
+    bulk_copy_g2s(smem_address(stage + plan.row_ptr), reinterpret_cast<const void*>(row_ptr.begin), row_ptr.bytes, full);
+  if (kBase && row_base.bytes)
+    bulk_copy_g2s(smem_address(stage + plan.row_base), reinterpret_cast<const void*>(row_base.begin), row_base.bytes, full);
+  if (kPacked && row_base.bytes) {
+    const AlignedRange<int> row_word(a.row_word, tile.x, tile.y);
+    bulk_copy_g2s(smem_address(stage + plan.row_word), reinterpret_cast<const void*>(row_word.begin), row_word.bytes, full);
+  }
+  if (kPacked && row_width.bytes)
+    bulk_copy_g2s(smem_address(stage + plan.row_width), reinterpret_cast<const void*>(row_width.begin), row_width.bytes, full);
+  if (values.bytes)
+    bulk_copy_g2s(smem_address(stage + plan.values), reinterpret_cast<const void*>(values.begin), values.bytes, full);
+  if (index.bytes)
+    bulk_copy_g2s(smem_address(stage + plan.index), reinterpret_cast<const void*>(index.begin), index.bytes, full);
+}
+
+// ---- k_spmv_tiles --------------------------------------------------------------------------------------
+// Per tile k (buffer s = k mod stages): every thread waits for the buffer's bulk copies, processes its
+// rows, and its warp then releases the buffer on the "empty" barrier; thread 0, once all eight warps have
+// released it, refills it with tile k + stages. Warps never wait for one another otherwise.
+template <class V, int LAYOUT, int T, int P>
+__global__ void __launch_bounds__(kTileBlock, 2) k_spmv_tiles(const KernelArgs a) {
+  static_assert(T % P == 0 && P >= 1 && P <= 32, "P must divide T");
+  if ((int64_t)blockIdx.x < a.vector_blocks) {   // rows longer than a tile, scheduled first
+    vector_rows<V, LAYOUT, T, kTileBlock>(a, blockIdx.x, a.vector_blocks);
+    return;
+  }
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_abort;
+  const StagePlan plan = stage_plan(a.tile_nnz, a.tile_rows, (int)sizeof(V), LAYOUT);
+  const int stages = a.stages;
+  const int64_t cta = (int64_t)blockIdx.x - a.vector_blocks;
+  const int64_t ctas = (int64_t)gridDim.x - a.vector_blocks;
+  const int64_t my_tiles = cta < a.tile_count ? (a.tile_count - cta + ctas - 1) / ctas : 0;
+  const uint32_t full0 = smem_address(smem), empty0 = full0 + 8 * kMaxStages;
+  unsigned char* buffers = smem + 64;
+  int64_t issued = 0;   // thread 0: tiles issued so far
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < stages; ++s) {
+      mbarrier_init(full0 + 8 * s, 1);
+      mbarrier_init(empty0 + 8 * s, kTileBlock / 32);
+    }
+    mbarrier_init_fence();
+    for (; issued < stages && issued < my_tiles; ++issued)
+      issue_tile<V, LAYOUT>(a, cta + issued * ctas, buffers + issued * plan.bytes, plan, full0 + 8 * (int)issued);
+  }
+  __syncthreads();
+
+  int64_t k = 0;
+  for (; k < my_tiles; ++k) {
+    const int s = (int)(k % stages);
+    const uint32_t phase = (uint32_t)((k / stages) & 1);
+    if (!mbarrier_wait_bounded(full0 + 8 * s, phase, 2000000000ull)) {
+      atomicExch(&s_abort, 1);
+      if (a.status) atomicOr(a.status, kStatusTimeout);
+    }
+    // leave together or not at all: the reduction's shuffles need every lane of the warp
+    if (__shfl_sync(0xffffffffu, *(volatile int*)&s_abort, 0)) break;
+    process_tile<V, LAYOUT, T, P>(a, buffers + s * plan.bytes, plan);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbarrier_arrive(empty0 + 8 * s);
+    if (threadIdx.x == 0 && issued < my_tiles) {
+      // refill this buffer with tile k + stages once every warp has released it
+      if (mbarrier_wait_bounded(empty0 + 8 * s, phase, 2000000000ull)) {
+        issue_tile<V, LAYOUT>(a, cta + issued * ctas, buffers + s * plan.bytes, plan, full0 + 8 * s);
+        ++issued;
+      } else {
+        atomicExch(&s_abort, 1);
+        if (a.status) atomicOr(a.status, kStatusTimeout);
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    // after an abort: wait, bounded, for the copies issued and not consumed before the CTA's shared
+    // memory is released
+    for (int64_t pending = k; pending < issued; ++pending)
+      mbarrier_wait_bounded(full0 + 8 * (int)(pending % stages), (uint32_t)((pending / stages) & 1), 100000000ull);
   }
 }
 

@@ -2,4 +2,5 @@
 #define VALUE_TYPE __half
 #define LAUNCH_TILES_NAME launch_tiles_f16
 #define LAUNCH_VECTOR_NAME launch_vector_f16
+#define TILES_OCCUPANCY_NAME tiles_occupancy_f16
 #include "kernels_instantiate.cuh"

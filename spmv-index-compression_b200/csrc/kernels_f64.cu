@@ -2,4 +2,5 @@
 #define VALUE_TYPE double
 #define LAUNCH_TILES_NAME launch_tiles_f64
 #define LAUNCH_VECTOR_NAME launch_vector_f64
+#define TILES_OCCUPANCY_NAME tiles_occupancy_f64
 #include "kernels_instantiate.cuh"

@@ -7,39 +7,63 @@ namespace {
 
 template <class V, int L, int T, int P>
 cudaError_t run_tiles(const KernelArgs& a, cudaStream_t stream) {
-  const TileSmem plan = tile_smem(a.tile_nnz, a.tile_rows, (int)sizeof(V), L);
-  if (plan.total > 48 * 1024) {
-    const cudaError_t status = cudaFuncSetAttribute(k_spmv_tiles<V, L, T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.total);
-    if (status != cudaSuccess) return status;
-  }
-  const int64_t blocks = a.vector_blocks + a.tile_count;
+  const int smem = tile_smem_bytes(a.tile_nnz, a.tile_rows, (int)sizeof(V), L, a.stages);
+  const int64_t blocks = a.vector_blocks + a.tile_ctas;
   if (blocks <= 0) return cudaSuccess;
-  k_spmv_tiles<V, L, T, P><<<(unsigned)blocks, kTileBlock, plan.total, stream>>>(a);
+  k_spmv_tiles<V, L, T, P><<<(unsigned)blocks, kTileBlock, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
+// Sets the shared-memory limit of the variant to smem and returns its resident CTAs per multiprocessor.
+template <class V, int L, int T, int P>
+cudaError_t occupancy_of(int smem, int* blocks) {
+  cudaError_t status = cudaFuncSetAttribute(k_spmv_tiles<V, L, T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (status != cudaSuccess) return status;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k_spmv_tiles<V, L, T, P>, kTileBlock, smem);
+}
+
+// mode 0: launch; mode 1: occupancy query into *blocks
+template <class V, int L, int T, int P>
+cudaError_t tiles_variant(int mode, const KernelArgs& a, cudaStream_t stream, int smem, int* blocks) {
+  return mode == 0 ? run_tiles<V, L, T, P>(a, stream) : occupancy_of<V, L, T, P>(smem, blocks);
+}
+
 template <class V, int L, int T>
-cudaError_t tiles_for_tpr(int physical_tpr, const KernelArgs& a, cudaStream_t stream) {
+cudaError_t tiles_for_tpr(int physical_tpr, int mode, const KernelArgs& a, cudaStream_t stream, int smem, int* blocks) {
   switch (T / physical_tpr) {
-    case 1: return run_tiles<V, L, T, T>(a, stream);
-    case 2: if constexpr (T >= 2) return run_tiles<V, L, T, T / 2>(a, stream); break;
-    case 4: if constexpr (T >= 4) return run_tiles<V, L, T, T / 4>(a, stream); break;
-    case 8: if constexpr (T >= 8) return run_tiles<V, L, T, T / 8>(a, stream); break;
-    case 16: if constexpr (T >= 16) return run_tiles<V, L, T, T / 16>(a, stream); break;
+    case 1: return tiles_variant<V, L, T, T>(mode, a, stream, smem, blocks);
+    case 2: if constexpr (T >= 2) return tiles_variant<V, L, T, T / 2>(mode, a, stream, smem, blocks); break;
+    case 4: if constexpr (T >= 4) return tiles_variant<V, L, T, T / 4>(mode, a, stream, smem, blocks); break;
+    case 8: if constexpr (T >= 8) return tiles_variant<V, L, T, T / 8>(mode, a, stream, smem, blocks); break;
+    case 16: if constexpr (T >= 16) return tiles_variant<V, L, T, T / 16>(mode, a, stream, smem, blocks); break;
     default: break;
   }
   return cudaErrorInvalidValue;
 }
 
 template <class V, int L>
-cudaError_t tiles_for_layout(int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream) {
+cudaError_t tiles_for_layout(int tpr, int physical_tpr, int mode, const KernelArgs& a, cudaStream_t stream, int smem, int* blocks) {
   if (!tile_variant_exists(tpr, physical_tpr)) return cudaErrorInvalidValue;
   switch (tpr) {
-    case 2: return tiles_for_tpr<V, L, 2>(physical_tpr, a, stream);
-    case 4: return tiles_for_tpr<V, L, 4>(physical_tpr, a, stream);
-    case 8: return tiles_for_tpr<V, L, 8>(physical_tpr, a, stream);
-    case 16: return tiles_for_tpr<V, L, 16>(physical_tpr, a, stream);
-    case 32: return tiles_for_tpr<V, L, 32>(physical_tpr, a, stream);
+    case 2: return tiles_for_tpr<V, L, 2>(physical_tpr, mode, a, stream, smem, blocks);
+    case 4: return tiles_for_tpr<V, L, 4>(physical_tpr, mode, a, stream, smem, blocks);
+    case 8: return tiles_for_tpr<V, L, 8>(physical_tpr, mode, a, stream, smem, blocks);
+    case 16: return tiles_for_tpr<V, L, 16>(physical_tpr, mode, a, stream, smem, blocks);
+    case 32: return tiles_for_tpr<V, L, 32>(physical_tpr, mode, a, stream, smem, blocks);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <class V>
+cudaError_t tiles_for_value(int layout, int tpr, int physical_tpr, int mode, const KernelArgs& a, cudaStream_t stream, int smem,
+                            int* blocks) {
+  switch (layout) {
+    case SPMV_LAYOUT_I32: return tiles_for_layout<V, SPMV_LAYOUT_I32>(tpr, physical_tpr, mode, a, stream, smem, blocks);
+    case SPMV_LAYOUT_I16: return tiles_for_layout<V, SPMV_LAYOUT_I16>(tpr, physical_tpr, mode, a, stream, smem, blocks);
+    case SPMV_LAYOUT_R16: return tiles_for_layout<V, SPMV_LAYOUT_R16>(tpr, physical_tpr, mode, a, stream, smem, blocks);
+    case SPMV_LAYOUT_LP:  return tiles_for_layout<V, SPMV_LAYOUT_LP>(tpr, physical_tpr, mode, a, stream, smem, blocks);
+    case SPMV_LAYOUT_I8:  return tiles_for_layout<V, SPMV_LAYOUT_I8>(tpr, physical_tpr, mode, a, stream, smem, blocks);
+    case SPMV_LAYOUT_R8:  return tiles_for_layout<V, SPMV_LAYOUT_R8>(tpr, physical_tpr, mode, a, stream, smem, blocks);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -66,15 +90,14 @@ cudaError_t vector_for_layout(int tpr, const KernelArgs& a, int64_t blocks, cuda
 }  // namespace
 
 cudaError_t LAUNCH_TILES_NAME(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream) {
-  switch (layout) {
-    case SPMV_LAYOUT_I32: return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_I32>(tpr, physical_tpr, a, stream);
-    case SPMV_LAYOUT_I16: return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_I16>(tpr, physical_tpr, a, stream);
-    case SPMV_LAYOUT_R16: return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_R16>(tpr, physical_tpr, a, stream);
-    case SPMV_LAYOUT_LP:  return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_LP>(tpr, physical_tpr, a, stream);
-    case SPMV_LAYOUT_I8:  return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_I8>(tpr, physical_tpr, a, stream);
-    case SPMV_LAYOUT_R8:  return tiles_for_layout<VALUE_TYPE, SPMV_LAYOUT_R8>(tpr, physical_tpr, a, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  return tiles_for_value<VALUE_TYPE>(layout, tpr, physical_tpr, 0, a, stream, 0, nullptr);
+}
+
+int TILES_OCCUPANCY_NAME(int layout, int tpr, int physical_tpr, int smem) {
+  int blocks = 0;
+  const KernelArgs unused{};
+  if (tiles_for_value<VALUE_TYPE>(layout, tpr, physical_tpr, 1, unused, nullptr, smem, &blocks) != cudaSuccess) return 0;
+  return blocks;
 }
 
 cudaError_t LAUNCH_VECTOR_NAME(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream) {

@@ -43,18 +43,19 @@ struct DeviceScope {
   }
 };
 
+// A device copy of count elements followed by kStreamPadding zero bytes, so that a tile's bulk copy may
+// round its end up to the next 16-byte boundary.
 template <class T>
 T* device_upload(const void* host, size_t count, int64_t& total_bytes) {
   T* device = nullptr;
-  if (count == 0) count = 1;   // keep every stream a valid pointer
-  cuda_check(cudaMalloc(reinterpret_cast<void**>(&device), sizeof(T) * count), "cudaMalloc");
-  total_bytes += (int64_t)(sizeof(T) * count);
-  if (host) {
-    const cudaError_t status = cudaMemcpy(device, host, sizeof(T) * count, cudaMemcpyHostToDevice);
-    if (status != cudaSuccess) {
-      cudaFree(device);
-      cuda_check(status, "cudaMemcpy");
-    }
+  const size_t bytes = sizeof(T) * count + kStreamPadding;
+  cuda_check(cudaMalloc(reinterpret_cast<void**>(&device), bytes), "cudaMalloc");
+  total_bytes += (int64_t)bytes;
+  cudaError_t status = cudaMemset(device, 0, bytes);
+  if (status == cudaSuccess && host && count) status = cudaMemcpy(device, host, sizeof(T) * count, cudaMemcpyHostToDevice);
+  if (status != cudaSuccess) {
+    cudaFree(device);
+    cuda_check(status, "device upload");
   }
   return device;
 }
@@ -105,11 +106,15 @@ TilePlan plan_tiles(const Csr& matrix, int tile_nnz, int tile_rows, const int* r
   return plan;
 }
 
-// Physical threads per row: about four nonzeros per thread in an average staged row, at least T/16.
-int choose_physical_tpr(int tpr, double mean_length) {
+// Physical threads per row P: as many as leave every row of a typical tile a group of its own (the
+// 256/P groups of a CTA take one row each per pass), at least T/16 (at most 16 lane sums per thread), and
+// at least T/8 for CSR-lp, whose decode holds more registers per lane. Measured on B200 with 4096-nonzero
+// tiles: P = 1 for 27-entry rows at T = 8, P = 2 for 33-entry rows.
+int choose_physical_tpr(int tpr, int layout, double rows_per_tile) {
   int physical = 1;
-  while (physical * 2 <= tpr && physical * 2 * 4 <= mean_length) physical *= 2;
-  while (tpr / physical > 16) physical *= 2;
+  while (physical * 2 <= tpr && (double)(kTileBlock / (physical * 2)) >= rows_per_tile) physical *= 2;
+  const int max_slots = layout == SPMV_LAYOUT_LP ? 8 : 16;
+  while (tpr / physical > max_slots) physical *= 2;
   return physical;
 }
 
@@ -117,7 +122,7 @@ int choose_physical_tpr(int tpr, double mean_length) {
 
 struct spmv_operator {
   int device = 0;
-  int layout = 0, dtype = 0, tpr = 0, physical_tpr = 0, tile_nnz = 0, tile_rows = 0;
+  int layout = 0, dtype = 0, tpr = 0, physical_tpr = 0, tile_nnz = 0, tile_rows = 0, stages = 0;
   int rows = 0, cols = 0;
   int64_t nnz = 0;
   spmv_memory memory{};
@@ -133,6 +138,7 @@ struct spmv_operator {
   int* long_rows = nullptr;
   unsigned* status = nullptr;
   int64_t tile_count = 0;
+  int64_t tile_ctas = 0;
   int64_t long_count = 0;
   int64_t device_bytes = 0;
 
@@ -154,6 +160,7 @@ namespace {
 KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   KernelArgs a{};
   a.rows = op->rows;
+  a.cols = op->cols;
   a.row_ptr = op->row_ptr;
   a.columns = op->columns;
   a.row_base = op->row_base;
@@ -168,6 +175,8 @@ KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   a.tile_count = op->tile_count;
   a.tile_nnz = op->tile_nnz;
   a.tile_rows = op->tile_rows;
+  a.stages = op->stages;
+  a.tile_ctas = op->tile_ctas;
   a.row_list = op->long_rows;
   a.row_count = op->long_count;
   a.vector_blocks = op->long_count > 0 ? (op->long_count * op->tpr + kTileBlock - 1) / kTileBlock : 0;
@@ -224,16 +233,26 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     op->cols = m.cols;
     op->nnz = m.nnz();
     op->memory = memory_of(m, facts, layout, dtype, tpr);
-    op->tile_nnz = config->tile_nnz > 0 ? config->tile_nnz : 2048;
-    op->tile_rows = std::max(64, op->tile_nnz / 2);
-    {
-      int shared_limit = 0;
-      cuda_check(cudaDeviceGetAttribute(&shared_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, op->device), "device attribute");
-      const TileSmem smem = tile_smem(op->tile_nnz, op->tile_rows, value_bytes, layout);
-      if (smem.total > shared_limit)
-        fail(SPMV_ERR_INVALID_ARGUMENT, "tile_nnz needs " + std::to_string(smem.total) + " bytes of shared memory, above the " +
-                                            std::to_string(shared_limit) + " a block may have");
+    op->tile_nnz = config->tile_nnz > 0 ? config->tile_nnz : 4096;
+    // rows of a tile at most: twice the rows of an average tile, so short-row tiles still fill up
+    const double mean_length = m.rows > 0 ? (double)m.nnz() / m.rows : 1.0;
+    op->tile_rows = std::max(64, std::min(std::max(64, op->tile_nnz), (int)(2.0 * op->tile_nnz / std::max(mean_length, 1.0)) + 16));
+    op->tile_rows = (op->tile_rows + 15) & ~15;
+    op->stages = config->stages > 0 ? config->stages : 2;
+    require(op->stages >= 1 && op->stages <= kMaxStages, "stages must be 0 or 1..4");
+    int shared_limit = 0, multiprocessors = 0;
+    cuda_check(cudaDeviceGetAttribute(&shared_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, op->device), "device attribute");
+    cuda_check(cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, op->device), "device attribute");
+    // the default tile halves until its buffers fit (a large tile_nnz is the caller's to size)
+    while (config->tile_nnz == 0 && op->tile_nnz > 256 &&
+           tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages) > shared_limit) {
+      op->tile_nnz /= 2;
+      op->tile_rows = std::max(64, (op->tile_rows / 2 + 15) & ~15);
     }
+    const int smem = tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages);
+    if (smem > shared_limit)
+      fail(SPMV_ERR_INVALID_ARGUMENT, "tiles need " + std::to_string(smem) + " bytes of shared memory, above the " +
+                                          std::to_string(shared_limit) + " a block may have");
 
     // encoded streams
     const size_t nnz = (size_t)m.nnz();
@@ -290,9 +309,14 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     op->long_rows = device_upload<int>(plan.long_rows.data(), plan.long_rows.size(), op->device_bytes);
     op->status = device_upload<unsigned>(nullptr, 1, op->device_bytes);
     cuda_check(cudaMemset(op->status, 0, sizeof(unsigned)), "cudaMemset");
-    const double mean = plan.short_rows > 0 ? (double)plan.short_nnz / (double)plan.short_rows : 0.0;
-    op->physical_tpr = config->physical_tpr > 0 ? config->physical_tpr : choose_physical_tpr(tpr, mean);
-    if (op->tile_count + (op->long_count * tpr + kTileBlock - 1) / kTileBlock > 0x7fffffff)
+    const double mean = plan.short_rows > 0 ? (double)plan.short_nnz / (double)plan.short_rows : 1.0;
+    const double rows_per_tile = std::min<double>(op->tile_rows, op->tile_nnz / std::max(mean, 1.0));
+    op->physical_tpr = config->physical_tpr > 0 ? config->physical_tpr : choose_physical_tpr(tpr, layout, rows_per_tile);
+    // persistent tile CTAs: as many as fit on the device at once, never more than there are tiles
+    const int resident = tiles_occupancy(dtype, layout, tpr, op->physical_tpr, smem);
+    if (resident <= 0 && op->tile_count > 0) fail(SPMV_ERR_CUDA, "tile kernel cannot be resident with this configuration");
+    op->tile_ctas = std::min<int64_t>(op->tile_count, (int64_t)resident * multiprocessors);
+    if (op->tile_ctas + (op->long_count * tpr + kTileBlock - 1) / kTileBlock > 0x7fffffff)
       fail(SPMV_ERR_TOO_LARGE, "grid exceeds 2^31-1 blocks");
     cuda_check(cudaDeviceSynchronize(), "operator upload");
     *out = op.release();
@@ -311,15 +335,27 @@ int spmv_operator_get_info(const spmv_operator* op, spmv_operator_info* info) {
     info->physical_tpr = op->physical_tpr;
     info->tile_nnz = op->tile_nnz;
     info->tiles = op->tile_count;
+    info->tile_ctas = op->tile_ctas;
+    info->stages = op->stages;
+    info->tile_rows = op->tile_rows;
     info->long_rows = op->long_count;
     info->device_bytes = op->device_bytes;
     info->memory = op->memory;
   });
 }
 
+// The tile kernel copies x with 4- or 8-byte asynchronous copies: x must be aligned to its element size,
+// and to 4 bytes for FP16.
+static void check_vector_alignment(const spmv_operator* op, const void* x, const void* y) {
+  const uintptr_t x_alignment = (uintptr_t)std::max(4, value_bytes_of(op->dtype));
+  require(((uintptr_t)x % x_alignment) == 0, "x must be aligned to its element size (4 bytes for FP16)");
+  require(((uintptr_t)y % (uintptr_t)value_bytes_of(op->dtype)) == 0, "y must be aligned to its element size");
+}
+
 int spmv_operator_run(const spmv_operator* op, const void* x, void* y, void* stream) {
   return guarded([&] {
     require(op && x && y, "op, x and y are required");
+    check_vector_alignment(op, x, y);
     const KernelArgs a = kernel_args(op, x, y);
     cuda_check(launch_tiles(op->dtype, op->layout, op->tpr, op->physical_tpr, a, static_cast<cudaStream_t>(stream)),
                "SpMV launch");
@@ -330,6 +366,7 @@ int spmv_operator_run_host(const spmv_operator* op, const void* x_host, void* y_
                            void* stream) {
   return guarded([&] {
     require(op && x_host && y_host && x_device && y_device, "all buffers are required");
+    check_vector_alignment(op, x_device, y_device);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t value_bytes = (size_t)value_bytes_of(op->dtype);
     cuda_check(cudaMemcpyAsync(x_device, x_host, value_bytes * op->cols, cudaMemcpyHostToDevice, s), "copy x");
@@ -352,8 +389,6 @@ int spmv_operator_check(const spmv_operator* op) {
     if (word & kStatusTimeout) {
       timed_out = 1;
       set_last_error("a bounded device-side wait gave up");
-    } else if (word & kStatusAlignment) {
-      set_last_error("a bulk copy was not 16-byte aligned and was replaced by plain loads");
     }
   });
   return status != SPMV_OK ? status : (timed_out ? SPMV_ERR_TIMEOUT : SPMV_OK);
@@ -386,6 +421,7 @@ int spmv_launch(int layout, int dtype, int tpr, const spmv_device_matrix* matrix
     if (layout == SPMV_LAYOUT_R16 || layout == SPMV_LAYOUT_R8) require(matrix->row_base != nullptr, "missing row_base");
     KernelArgs a{};
     a.rows = matrix->rows;
+    a.cols = matrix->cols;
     a.row_ptr = matrix->row_ptr;
     a.columns = matrix->columns;
     a.row_base = matrix->row_base;

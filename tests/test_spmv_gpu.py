@@ -198,6 +198,20 @@ def test_cusparse_agrees_within_tolerance(ragged, dtype):
     assert l2_relative(y, reference_y) <= CUSPARSE_TOLERANCE[dtype]
 
 
+def test_misaligned_vectors_are_refused(ragged):
+    with spmv.Operator(ragged, spmv.I32, spmv.F64, 8) as op:
+        x = torch.zeros(ragged.cols + 1, dtype=torch.float64, device="cuda")
+        y = torch.zeros(ragged.rows + 1, dtype=torch.float64, device="cuda")
+        with pytest.raises(spmv.SpmvError) as failure:
+            op.run(x.data_ptr() + 4, y.data_ptr())
+        assert failure.value.status == spmv.ERR_INVALID_ARGUMENT
+    with spmv.Operator(ragged, spmv.I32, spmv.F16, 8) as op:
+        x = torch.zeros(ragged.cols + 1, dtype=torch.float16, device="cuda")
+        y = torch.zeros(ragged.rows, dtype=torch.float16, device="cuda")
+        with pytest.raises(spmv.SpmvError):
+            op.run(x.data_ptr() + 2, y.data_ptr())
+
+
 def test_streams_and_repeated_runs(ragged):
     """Products on a side stream, repeated, with the same bits every time."""
     x = spmv.fill_uniform(spmv.F64, ragged.cols, 1)
