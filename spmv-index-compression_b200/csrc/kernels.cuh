@@ -18,10 +18,10 @@
 //                  nonzeros fit in shared memory). Each CTA owns tiles cta, cta + ctas, ... and keeps a
 //                  ring of `stages` shared-memory buffers: thread 0 streams upcoming tiles into free
 //                  buffers with cp.async.bulk (the 1-D TMA engine), completing on the buffer's "full"
-//                  mbarrier. On a resident tile every thread gathers x at up to 32 of its entries' decoded
-//                  columns at once into registers and adds them into its lane chains, reading values and
-//                  columns from shared memory; its warp then releases the buffer on the "empty" mbarrier
-//                  and thread 0 refills it with a later tile. The operator
+//                  mbarrier. On a resident tile every thread decodes its entries' columns, gathers x at
+//                  up to 32 of them at once into registers and adds them into its lane chains, reading
+//                  values from shared memory; the last warp to
+//                  finish with a buffer refills it with a later tile. The operator
 //                  pads every stream by 16 bytes, so each bulk copy is the 16-byte-aligned superset of a
 //                  tile's range. Its leading `vector_blocks` CTAs run the vector path over rows longer
 //                  than a tile.
@@ -42,6 +42,7 @@ constexpr int kVectorBlock = 128;          // threads of a vector CTA
 constexpr int kMaxStages = 4;              // shared-memory buffers of a tile CTA at most
 constexpr int kStreamPadding = 16;         // bytes every operator stream carries past its end
 constexpr unsigned kStatusTimeout = 1u;    // bit of the status word: a bounded wait gave up
+constexpr unsigned kStatusSmem = 2u;       // bit: a long-row chunk did not fit the launch's shared memory
 
 // ---- value types --------------------------------------------------------------------------------
 template <class V> struct ValueTraits;
@@ -97,13 +98,15 @@ struct KernelArgs {
   int stages;                // shared-memory buffers of a tile CTA (1..kMaxStages)
   const int* row_list;       // rows of the vector path (nullptr: rows 0..row_count-1)
   int64_t row_count;         // entries of row_list, or rows
-  int64_t vector_blocks;     // k_spmv_tiles: its first vector_blocks CTAs run the vector path on row_list
+  int64_t vector_blocks;     // k_spmv_tiles: its first vector_blocks CTAs take the rows of row_list
+  int long_chunk;            // k_spmv_tiles: entries per chunk of a long row (a multiple of kTileBlock)
+  int smem_bytes;            // k_spmv_tiles: dynamic shared memory of the launch
   int64_t tile_ctas;         // k_spmv_tiles: persistent CTAs over the tiles after the vector blocks
   unsigned* status;          // device status word (may be null)
 };
 
 // ---- shared-memory plan of a tile CTA (host and device compute it alike) ----------------------------
-// [0, 64): full[kMaxStages] and empty[kMaxStages] mbarriers; then `stages` buffers, each a header (the
+// [0, 64): full[kMaxStages] mbarriers; then `stages` buffers, each a header (the
 // tile's rows and image origins) and 16-byte-aligned images of the tile's row_ptr, row_base, row_word and
 // row_width slices and of its value and index (or CSR-lp word) ranges. An image starts at the 16-byte
 // boundary at or below its first element, so it holds up to 16 bytes before and after the range.
@@ -346,9 +349,9 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
   constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
   constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
   constexpr int S = T / P;
-  // x values gathered at once per thread: 32, or 16 for FP64 when 16 lane sums or the CSR-lp decode
-  // already hold many registers (two CTAs of 256 threads per multiprocessor leave 128 per thread)
-  constexpr int kBatch = (sizeof(V) == 8 && (S >= 16 || kPacked)) ? kGathers / 2 : kGathers;
+  // x values gathered at once per thread: 32, or 16 for FP64 when 16 lane sums (or 8 CSR-lp lanes with
+  // their running columns) already hold many of the 128 registers two CTAs of 256 threads leave a thread
+  constexpr int kBatch = (sizeof(V) == 8 && (S >= 16 || (kPacked && S >= 8))) ? kGathers / 2 : kGathers;
   constexpr int R = S >= kBatch ? 1 : kBatch / S;
   constexpr int kGroups = kTileBlock / P;
   const TileView<V, LAYOUT> tile(stage, plan);
@@ -384,37 +387,38 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
             }
         }
       } else {
+        // lane p + j*P owns quotient (+1 below remainder) deltas from bit width * (lane * quotient +
+        // min(lane, remainder)); both are recomputed where used, so only the running columns stay live
         const int length = entry_end - entry_begin;
         const int quotient = length / T, remainder = length - quotient * T;
         const uint32_t width = tile.row_width[row];
         const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
         const uint32_t* words = reinterpret_cast<const uint32_t*>(tile.index) + tile.row_word[row];
-        uint32_t start[S];
-        int column[S], mine[S];
+        int column[S];
 #pragma unroll
-        for (int j = 0; j < S; ++j) {
-          const int lane = p + j * P;
-          mine[j] = quotient + (lane < remainder ? 1 : 0);
-          start[j] = width * (uint32_t)(lane * quotient + (lane < remainder ? lane : remainder));
-          column[j] = tile.row_base[row];
-        }
+        for (int j = 0; j < S; ++j) column[j] = tile.row_base[row];
         const int rounds = quotient + (remainder > 0 ? 1 : 0);
         for (int round = 0; round < rounds; round += R) {
           V xv[R][S];
 #pragma unroll
           for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int j = 0; j < S; ++j)
-              if (round + r < mine[j]) {
-                column[j] += (int)packed_delta(words, start[j] + (uint32_t)(round + r) * width, mask);
+            for (int j = 0; j < S; ++j) {
+              const int lane = p + j * P;
+              if (round + r < quotient + (lane < remainder ? 1 : 0)) {
+                const uint32_t delta = (uint32_t)(lane * quotient + (lane < remainder ? lane : remainder) + round + r);
+                column[j] += (int)packed_delta(words, delta * width, mask);
                 xv[r][j] = load_readonly(x + column[j]);
               }
+            }
 #pragma unroll
           for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int j = 0; j < S; ++j)
-              if (round + r < mine[j])
-                acc[j] = VT::fma(VT::widen(tile.values[entry_begin + p + j * P + (round + r) * T]), VT::widen(xv[r][j]), acc[j]);
+            for (int j = 0; j < S; ++j) {
+              const int lane = p + j * P;
+              if (round + r < quotient + (lane < remainder ? 1 : 0))
+                acc[j] = VT::fma(VT::widen(tile.values[entry_begin + lane + (round + r) * T]), VT::widen(xv[r][j]), acc[j]);
+            }
         }
       }
     }
@@ -472,45 +476,120 @@ __device__ __forceinline__ void issue_tile(const KernelArgs& a, int64_t tile_id,
     bulk_copy_g2s(smem_address(stage + plan.index), reinterpret_cast<const void*>(index.begin), index.bytes, full);
 }
 
+// ---- rows longer than a tile ----------------------------------------------------------------------------
+// A row of the long-row list takes a whole CTA, chunk by chunk (a chunk starts at a multiple of T within
+// the row, so an entry keeps its lane). Per chunk: for CSR-lp, the T lane owners decode their chains'
+// columns into shared memory; then all threads load the chunk's values and gather x at its columns into
+// shared memory, every load independent of the others; then the T lane owners add the chunk into their
+// lane sums in order. The lane sums finish in the width-T shuffle tree of warp 0.
+template <class V, int LAYOUT, int T>
+__device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* smem, int64_t block, int64_t blocks) {
+  using VT = ValueTraits<V>;
+  using Acc = typename VT::Acc;
+  using Index = typename LayoutTraits<LAYOUT>::Index;
+  constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
+  constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
+  const int chunk = a.long_chunk;   // entries per chunk: a multiple of kTileBlock (and so of T)
+  if ((int64_t)chunk * (2 * (int)sizeof(V) + 4) > a.smem_bytes) {   // never by construction
+    if (threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusSmem);
+    return;
+  }
+  V* s_values = reinterpret_cast<V*>(smem);
+  V* s_x = s_values + chunk;
+  int* s_columns = reinterpret_cast<int*>(s_x + chunk);
+  const V* values = static_cast<const V*>(a.values);
+  const V* x = static_cast<const V*>(a.x);
+  const Index* index = static_cast<const Index*>(a.columns);
+  V* y = static_cast<V*>(a.y);
+  const int lane = threadIdx.x;   // lane owner when < T
+
+  for (int64_t item = block; item < a.row_count; item += blocks) {
+    const int row = a.row_list[item];
+    const int64_t begin = a.row_ptr[row], length = a.row_ptr[row + 1] - begin;
+    const int base = kBase ? a.row_base[row] : 0;
+    Acc sum = Acc(0);
+    // CSR-lp lane state (owners only): the next delta's bit and the running column
+    const int quotient = (int)(length / T), remainder = (int)(length - (int64_t)quotient * T);
+    const uint32_t width = kPacked ? a.row_width[row] : 0u;
+    const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
+    const uint32_t* words = kPacked ? a.words + a.row_word[row] : nullptr;
+    uint64_t bit = kPacked && lane < T ? (uint64_t)width * (uint64_t)(lane * quotient + (lane < remainder ? lane : remainder)) : 0;
+    int column = base;
+
+    for (int64_t first = 0; first < length; first += chunk) {
+      const int count = (int)(length - first < chunk ? length - first : chunk);
+      if constexpr (kPacked) {
+        if (lane < T) {
+          for (int i = lane; i < count; i += T, bit += width) {
+            const uint64_t w = bit >> 5;
+            column += (int)(__funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1), (uint32_t)(bit & 31)) & mask);
+            s_columns[i] = column;
+          }
+        }
+        __syncthreads();
+      }
+#pragma unroll 8
+      for (int i = threadIdx.x; i < count; i += kTileBlock) {
+        const int64_t e = begin + first + i;
+        const int c = kPacked ? s_columns[i] : base + (int)load_readonly(index + e);
+        s_values[i] = load_readonly(values + e);
+        s_x[i] = load_readonly(x + c);
+      }
+      __syncthreads();
+      if (lane < T)
+        for (int i = lane; i < count; i += T) sum = VT::fma(VT::widen(s_values[i]), VT::widen(s_x[i]), sum);
+      __syncthreads();
+    }
+    if (threadIdx.x < 32) {
+#pragma unroll
+      for (int offset = T / 2; offset > 0; offset >>= 1) sum = VT::add(sum, __shfl_down_sync(0xffffffffu, sum, offset, T));
+      if (threadIdx.x == 0) y[row] = VT::narrow(sum);
+    }
+  }
+}
+
 // ---- k_spmv_tiles --------------------------------------------------------------------------------------
-// Per tile k (buffer s = k mod stages): every thread waits for the buffer's bulk copies, processes its
-// rows, and its warp then releases the buffer on the "empty" barrier; thread 0, once all eight warps have
-// released it, refills it with tile k + stages. Warps never wait for one another otherwise.
+// Per tile k (buffer s = k mod stages): every thread waits for the buffer's bulk copies and processes its
+// rows; each warp then counts itself out of the buffer, and the last warp out refills it at once with
+// tile k + stages. No warp ever waits for another, nor for a producer.
 template <class V, int LAYOUT, int T, int P>
 __global__ void __launch_bounds__(kTileBlock, 2) k_spmv_tiles(const KernelArgs a) {
   static_assert(T % P == 0 && P >= 1 && P <= 32, "P must divide T");
+  constexpr int kWarps = kTileBlock / 32;
+  extern __shared__ __align__(128) unsigned char smem[];
   if ((int64_t)blockIdx.x < a.vector_blocks) {   // rows longer than a tile, scheduled first
-    vector_rows<V, LAYOUT, T, kTileBlock>(a, blockIdx.x, a.vector_blocks);
+    long_rows<V, LAYOUT, T>(a, smem, blockIdx.x, a.vector_blocks);
     return;
   }
-  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_abort;
+  __shared__ int s_released[kMaxStages];   // warps done with the buffer's current tile
+  __shared__ int s_fills[kMaxStages];      // bulk fills issued into the buffer so far
   const StagePlan plan = stage_plan(a.tile_nnz, a.tile_rows, (int)sizeof(V), LAYOUT);
   const int stages = a.stages;
   const int64_t cta = (int64_t)blockIdx.x - a.vector_blocks;
   const int64_t ctas = (int64_t)gridDim.x - a.vector_blocks;
   const int64_t my_tiles = cta < a.tile_count ? (a.tile_count - cta + ctas - 1) / ctas : 0;
-  const uint32_t full0 = smem_address(smem), empty0 = full0 + 8 * kMaxStages;
+  const uint32_t full0 = smem_address(smem);
   unsigned char* buffers = smem + 64;
-  int64_t issued = 0;   // thread 0: tiles issued so far
 
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int s = 0; s < stages; ++s) {
       mbarrier_init(full0 + 8 * s, 1);
-      mbarrier_init(empty0 + 8 * s, kTileBlock / 32);
+      s_released[s] = 0;
+      s_fills[s] = 0;
     }
     mbarrier_init_fence();
-    for (; issued < stages && issued < my_tiles; ++issued)
-      issue_tile<V, LAYOUT>(a, cta + issued * ctas, buffers + issued * plan.bytes, plan, full0 + 8 * (int)issued);
+    for (int s = 0; s < stages && s < my_tiles; ++s) {
+      issue_tile<V, LAYOUT>(a, cta + s * ctas, buffers + s * plan.bytes, plan, full0 + 8 * s);
+      s_fills[s] = 1;
+    }
   }
   __syncthreads();
 
-  int64_t k = 0;
-  for (; k < my_tiles; ++k) {
+  for (int64_t k = 0; k < my_tiles; ++k) {
     const int s = (int)(k % stages);
-    const uint32_t phase = (uint32_t)((k / stages) & 1);
-    if (!mbarrier_wait_bounded(full0 + 8 * s, phase, 2000000000ull)) {
+    if (!mbarrier_wait_bounded(full0 + 8 * s, (uint32_t)((k / stages) & 1), 2000000000ull)) {
       atomicExch(&s_abort, 1);
       if (a.status) atomicOr(a.status, kStatusTimeout);
     }
@@ -518,23 +597,24 @@ __global__ void __launch_bounds__(kTileBlock, 2) k_spmv_tiles(const KernelArgs a
     if (__shfl_sync(0xffffffffu, *(volatile int*)&s_abort, 0)) break;
     process_tile<V, LAYOUT, T, P>(a, buffers + s * plan.bytes, plan);
     __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbarrier_arrive(empty0 + 8 * s);
-    if (threadIdx.x == 0 && issued < my_tiles) {
-      // refill this buffer with tile k + stages once every warp has released it
-      if (mbarrier_wait_bounded(empty0 + 8 * s, phase, 2000000000ull)) {
-        issue_tile<V, LAYOUT>(a, cta + issued * ctas, buffers + s * plan.bytes, plan, full0 + 8 * s);
-        ++issued;
-      } else {
-        atomicExch(&s_abort, 1);
-        if (a.status) atomicOr(a.status, kStatusTimeout);
+    if ((threadIdx.x & 31) == 0) {
+      __threadfence_block();   // this warp's reads of the buffer happen before its release
+      if (atomicAdd(&s_released[s], 1) == kWarps - 1) {
+        __threadfence_block();
+        s_released[s] = 0;
+        if (k + stages < my_tiles) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue_tile<V, LAYOUT>(a, cta + (k + stages) * ctas, buffers + s * plan.bytes, plan, full0 + 8 * s);
+          atomicAdd(&s_fills[s], 1);
+        }
       }
     }
   }
-  if (threadIdx.x == 0) {
-    // after an abort: wait, bounded, for the copies issued and not consumed before the CTA's shared
-    // memory is released
-    for (int64_t pending = k; pending < issued; ++pending)
-      mbarrier_wait_bounded(full0 + 8 * (int)(pending % stages), (uint32_t)((pending / stages) & 1), 100000000ull);
+  __syncthreads();
+  if (threadIdx.x == 0 && s_abort) {
+    // after an abort: wait, bounded, for each buffer's last fill before the CTA's shared memory is released
+    for (int s = 0; s < stages; ++s)
+      if (s_fills[s] > 0) mbarrier_wait_bounded(full0 + 8 * s, (uint32_t)((s_fills[s] - 1) & 1), 100000000ull);
   }
 }
 

@@ -7,7 +7,7 @@ namespace {
 
 template <class V, int L, int T, int P>
 cudaError_t run_tiles(const KernelArgs& a, cudaStream_t stream) {
-  const int smem = tile_smem_bytes(a.tile_nnz, a.tile_rows, (int)sizeof(V), L, a.stages);
+  const int smem = a.smem_bytes;
   const int64_t blocks = a.vector_blocks + a.tile_ctas;
   if (blocks <= 0) return cudaSuccess;
   k_spmv_tiles<V, L, T, P><<<(unsigned)blocks, kTileBlock, smem, stream>>>(a);

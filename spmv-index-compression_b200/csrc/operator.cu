@@ -107,14 +107,14 @@ TilePlan plan_tiles(const Csr& matrix, int tile_nnz, int tile_rows, const int* r
 }
 
 // Physical threads per row P: as many as leave every row of a typical tile a group of its own (the
-// 256/P groups of a CTA take one row each per pass), at least T/16 (at most 16 lane sums per thread), and
-// at least T/8 for CSR-lp, whose decode holds more registers per lane. Measured on B200 with 4096-nonzero
-// tiles: P = 1 for 27-entry rows at T = 8, P = 2 for 33-entry rows.
+// 256/P groups of a CTA take one row each per pass), and at least T/16 (at most 16 lane sums per
+// thread). Measured on B200 with 4096-nonzero tiles: P = 1 for 27-entry rows at T = 8, P = 2 for
+// 33-entry rows.
 int choose_physical_tpr(int tpr, int layout, double rows_per_tile) {
   int physical = 1;
   while (physical * 2 <= tpr && (double)(kTileBlock / (physical * 2)) >= rows_per_tile) physical *= 2;
-  const int max_slots = layout == SPMV_LAYOUT_LP ? 8 : 16;
-  while (tpr / physical > max_slots) physical *= 2;
+  (void)layout;
+  while (tpr / physical > 16) physical *= 2;
   return physical;
 }
 
@@ -140,6 +140,9 @@ struct spmv_operator {
   int64_t tile_count = 0;
   int64_t tile_ctas = 0;
   int64_t long_count = 0;
+  int64_t long_ctas = 0;
+  int long_chunk = 0;
+  int smem_bytes = 0;
   int64_t device_bytes = 0;
 
   ~spmv_operator() {
@@ -179,7 +182,9 @@ KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   a.tile_ctas = op->tile_ctas;
   a.row_list = op->long_rows;
   a.row_count = op->long_count;
-  a.vector_blocks = op->long_count > 0 ? (op->long_count * op->tpr + kTileBlock - 1) / kTileBlock : 0;
+  a.vector_blocks = op->long_ctas;
+  a.long_chunk = op->long_chunk;
+  a.smem_bytes = op->smem_bytes;
   a.status = op->status;
   return a;
 }
@@ -243,11 +248,19 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     int shared_limit = 0, multiprocessors = 0;
     cuda_check(cudaDeviceGetAttribute(&shared_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, op->device), "device attribute");
     cuda_check(cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, op->device), "device attribute");
-    // the default tile halves until its buffers fit (a large tile_nnz is the caller's to size)
-    while (config->tile_nnz == 0 && op->tile_nnz > 256 &&
-           tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages) > shared_limit) {
-      op->tile_nnz /= 2;
-      op->tile_rows = std::max(64, (op->tile_rows / 2 + 15) & ~15);
+    // default tile: the largest multiple of 256 nonzeros, up to 4096, whose buffers let two CTAs share a
+    // multiprocessor (the register budget of k_spmv_tiles is sized for two)
+    if (config->tile_nnz == 0) {
+      int per_sm = 0;
+      cuda_check(cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, op->device), "device attribute");
+      const int budget = per_sm / 2 - 1024 - 1024;   // per CTA: minus the reserved and static shared memory
+      auto rows_for = [&](int tile_nnz) {
+        const int rows = std::max(64, std::min(std::max(64, tile_nnz), (int)(2.0 * tile_nnz / std::max(mean_length, 1.0)) + 16));
+        return (rows + 15) & ~15;
+      };
+      while (op->tile_nnz > 256 && tile_smem_bytes(op->tile_nnz, rows_for(op->tile_nnz), value_bytes, layout, op->stages) > budget)
+        op->tile_nnz -= 256;
+      op->tile_rows = rows_for(op->tile_nnz);
     }
     const int smem = tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages);
     if (smem > shared_limit)
@@ -312,12 +325,19 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     const double mean = plan.short_rows > 0 ? (double)plan.short_nnz / (double)plan.short_rows : 1.0;
     const double rows_per_tile = std::min<double>(op->tile_rows, op->tile_nnz / std::max(mean, 1.0));
     op->physical_tpr = config->physical_tpr > 0 ? config->physical_tpr : choose_physical_tpr(tpr, layout, rows_per_tile);
+    // long rows: one CTA per row at a time; a chunk of a long row (values, gathered x and, for CSR-lp,
+    // decoded columns) lives in the CTA's shared memory, at least kTileBlock entries, at most 8192, and
+    // the launch gets the larger of the tile buffers and one chunk
+    op->long_chunk = std::max(kTileBlock, std::min(8192, (smem / (2 * value_bytes + 4)) / kTileBlock * kTileBlock));
+    op->smem_bytes = std::max(smem, op->long_count > 0 ? op->long_chunk * (2 * value_bytes + 4) : 0);
+    if (op->smem_bytes > shared_limit) fail(SPMV_ERR_INVALID_ARGUMENT, "long-row chunk exceeds the shared memory of a block");
     // persistent tile CTAs: as many as fit on the device at once, never more than there are tiles
-    const int resident = tiles_occupancy(dtype, layout, tpr, op->physical_tpr, smem);
-    if (resident <= 0 && op->tile_count > 0) fail(SPMV_ERR_CUDA, "tile kernel cannot be resident with this configuration");
-    op->tile_ctas = std::min<int64_t>(op->tile_count, (int64_t)resident * multiprocessors);
-    if (op->tile_ctas + (op->long_count * tpr + kTileBlock - 1) / kTileBlock > 0x7fffffff)
-      fail(SPMV_ERR_TOO_LARGE, "grid exceeds 2^31-1 blocks");
+    const int resident = tiles_occupancy(dtype, layout, tpr, op->physical_tpr, op->smem_bytes);
+    if (resident <= 0 && (op->tile_count > 0 || op->long_count > 0))
+      fail(SPMV_ERR_CUDA, "tile kernel cannot be resident with this configuration");
+    op->tile_ctas = std::min<int64_t>(op->tile_count, (int64_t)std::max(1, resident) * multiprocessors);
+    op->long_ctas = std::min<int64_t>(op->long_count, (int64_t)std::max(1, resident) * multiprocessors);
+    if (op->tile_ctas + op->long_ctas > 0x7fffffff) fail(SPMV_ERR_TOO_LARGE, "grid exceeds 2^31-1 blocks");
     cuda_check(cudaDeviceSynchronize(), "operator upload");
     *out = op.release();
   });
@@ -390,6 +410,7 @@ int spmv_operator_check(const spmv_operator* op) {
       timed_out = 1;
       set_last_error("a bounded device-side wait gave up");
     }
+    if (word & kStatusSmem) fail(SPMV_ERR_CUDA, "a long-row chunk did not fit the launch's shared memory");
   });
   return status != SPMV_OK ? status : (timed_out ? SPMV_ERR_TIMEOUT : SPMV_OK);
 }

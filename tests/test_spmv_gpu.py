@@ -44,7 +44,7 @@ def physical_variants(tpr):
 
 @pytest.fixture(scope="module")
 def ragged():
-    """Ragged rows: empty rows, rows of 1..60, a few rows longer than any tile (2048 default)."""
+    """Ragged rows: empty rows, rows of 0..59 entries and three rows of 2049..2500 entries."""
     rows, cols = 3000, 2500
     row_ptr, col_ind, values = random_csr(rows, cols, lambda rng: rng.integers(0, 60), 7, empty_every=23,
                                           long_rows={11: 2400, 1500: 2049, 2999: 2500})
@@ -59,8 +59,12 @@ def test_operator_matches_oracle_every_layout(ragged, dtype, tpr):
         if not admissible(ragged, layout, tpr):
             continue
         expected = oracle_product(ragged, x, dtype, layout, tpr)
-        with spmv.Operator(ragged, layout, dtype, tpr) as op:
+        # 2048-nonzero tiles leave the three rows of 2049..2500 entries to the long-row path
+        with spmv.Operator(ragged, layout, dtype, tpr, tile_nnz=2048) as op:
             assert op.info().long_rows == 3
+            y = device_run(op, x)
+        assert np.array_equal(bits(y), bits(expected)), (spmv.LAYOUT_NAMES[layout], tpr)
+        with spmv.Operator(ragged, layout, dtype, tpr) as op:   # the library's own tile plan
             y = device_run(op, x)
         assert np.array_equal(bits(y), bits(expected)), (spmv.LAYOUT_NAMES[layout], tpr)
 
