@@ -108,13 +108,14 @@ TilePlan plan_tiles(const Csr& matrix, int tile_nnz, int tile_rows, const int* r
 
 // Physical threads per row P: as many as leave every row of a typical tile a group of its own (the
 // 256/P groups of a CTA take one row each per pass), and at least T/16 (at most 16 lane sums per
-// thread). Measured on B200 with 4096-nonzero tiles: P = 1 for 27-entry rows at T = 8, P = 2 for
-// 33-entry rows.
+// thread; T/8 for CSR-lp, whose 16-lane variants gather half as deep). Measured on B200 with
+// 4096-nonzero tiles: P = 1 for 27-entry rows at T = 8, P = 2 for 33-entry rows, P = 4 for CSR-lp at
+// T = 32.
 int choose_physical_tpr(int tpr, int layout, double rows_per_tile) {
   int physical = 1;
   while (physical * 2 <= tpr && (double)(kTileBlock / (physical * 2)) >= rows_per_tile) physical *= 2;
-  (void)layout;
-  while (tpr / physical > 16) physical *= 2;
+  const int max_slots = layout == SPMV_LAYOUT_LP ? 8 : 16;
+  while (tpr / physical > max_slots) physical *= 2;
   return physical;
 }
 
