@@ -288,6 +288,11 @@ int spmv_comm_unique_id(void* id128);
 int spmv_comm_create(int nranks, int rank, const void* id128, int device, spmv_comm** out);
 void spmv_comm_destroy(spmv_comm* comm);
 
+/* Waits until the stream's work is done or a collective failed, for at most timeout_ms. On an NCCL
+ * error (SPMV_ERR_NCCL) or the timeout (SPMV_ERR_TIMEOUT) the communicator is marked aborted and
+ * spmv_comm_destroy aborts it instead of waiting for the other ranks. */
+int spmv_comm_check(spmv_comm* comm, void* stream, int timeout_ms);
+
 /* Chained products y -> x over the row shards: each rank holds the operator of its rows
  * (shard_row_begin[rank] .. shard_row_begin[rank+1]) and the full x. Every product computes the rank's y
  * shard into its slice of the next x, then all-gathers the slices over NCCL, products times. x_current

@@ -1,0 +1,190 @@
+// multi.cpp — the multi-GPU layer: an NCCL communicator over the ranks of a job (one process per GPU)
+// and chained products over nnz-balanced row shards with x replicated.
+//
+// A chained product y -> x: every rank multiplies its row shard into its slice of the next x, then the
+// slices are all-gathered. Shards differ in size after nnz balancing, so the all-gather is a group of
+// in-place broadcasts, one per rank (an all-gather of unequal pieces). NCCL is opened at run time
+// (dlopen, reusing a libnccl.so.2 the process already loaded, e.g. PyTorch's), so the library does not
+// pin an NCCL version of its own.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <mutex>
+#include <thread>
+
+#include "capi_internal.hpp"
+
+namespace spmvb200 {
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*group_start)() = nullptr;
+  ncclResult_t (*group_end)() = nullptr;
+  ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*get_error_string)(ncclResult_t) = nullptr;
+  bool loaded = false;
+};
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* handle = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!handle) handle = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!handle) handle = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!handle) return;
+    bool ok = true;
+    auto bind = [&](auto& pointer, const char* name) {
+      pointer = reinterpret_cast<std::remove_reference_t<decltype(pointer)>>(dlsym(handle, name));
+      ok = ok && pointer != nullptr;
+    };
+    bind(api.get_unique_id, "ncclGetUniqueId");
+    bind(api.comm_init_rank, "ncclCommInitRank");
+    bind(api.comm_destroy, "ncclCommDestroy");
+    bind(api.comm_abort, "ncclCommAbort");
+    bind(api.comm_get_async_error, "ncclCommGetAsyncError");
+    bind(api.group_start, "ncclGroupStart");
+    bind(api.group_end, "ncclGroupEnd");
+    bind(api.broadcast, "ncclBroadcast");
+    bind(api.get_error_string, "ncclGetErrorString");
+    api.loaded = ok;
+  });
+  if (!api.loaded) fail(SPMV_ERR_NCCL, "NCCL (libnccl.so.2) could not be loaded");
+  return api;
+}
+
+void nccl_check(ncclResult_t result, const char* what) {
+  if (result == ncclSuccess) return;
+  fail(SPMV_ERR_NCCL, std::string(what) + ": " + nccl().get_error_string(result));
+}
+
+ncclDataType_t nccl_type(int dtype) {
+  switch (dtype) {
+    case SPMV_F64: return ncclFloat64;
+    case SPMV_F32: return ncclFloat32;
+    default: return ncclFloat16;
+  }
+}
+
+}  // namespace
+}  // namespace spmvb200
+
+struct spmv_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 0;
+  int rank = 0;
+  int device = 0;
+  bool aborted = false;
+};
+
+using namespace spmvb200;
+
+extern "C" {
+
+int spmv_comm_unique_id(void* id128) {
+  return guarded([&] {
+    require(id128 != nullptr, "id128 is required");
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+    ncclUniqueId id;
+    nccl_check(nccl().get_unique_id(&id), "ncclGetUniqueId");
+    std::memcpy(id128, &id, sizeof(id));
+  });
+}
+
+int spmv_comm_create(int nranks, int rank, const void* id128, int device, spmv_comm** out) {
+  return guarded([&] {
+    require(out && id128 && nranks >= 1 && rank >= 0 && rank < nranks, "bad communicator arguments");
+    *out = nullptr;
+    std::unique_ptr<spmv_comm> comm(new spmv_comm);
+    comm->nranks = nranks;
+    comm->rank = rank;
+    if (device >= 0) {
+      const cudaError_t status = cudaSetDevice(device);
+      if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(status));
+    }
+    cudaGetDevice(&comm->device);
+    ncclUniqueId id;
+    std::memcpy(&id, id128, sizeof(id));
+    nccl_check(nccl().comm_init_rank(&comm->comm, nranks, id, rank), "ncclCommInitRank");
+    *out = comm.release();
+  });
+}
+
+void spmv_comm_destroy(spmv_comm* comm) {
+  if (!comm) return;
+  if (comm->comm) {
+    if (comm->aborted) nccl().comm_abort(comm->comm);
+    else nccl().comm_destroy(comm->comm);
+  }
+  delete comm;
+}
+
+// Waits until the stream's work is done or a collective failed, for at most timeout_ms; on an NCCL error
+// or the timeout the communicator is aborted (so that no rank stays blocked) and the call fails.
+int spmv_comm_check(spmv_comm* comm, void* stream, int timeout_ms) {
+  return guarded([&] {
+    require(comm && comm->comm, "comm is required");
+    const auto start = std::chrono::steady_clock::now();
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (;;) {
+      ncclResult_t async = ncclSuccess;
+      nccl_check(nccl().comm_get_async_error(comm->comm, &async), "ncclCommGetAsyncError");
+      if (async != ncclSuccess && async != ncclInProgress) {
+        comm->aborted = true;
+        fail(SPMV_ERR_NCCL, std::string("collective failed: ") + nccl().get_error_string(async));
+      }
+      const cudaError_t query = cudaStreamQuery(s);
+      if (query == cudaSuccess) return;
+      if (query != cudaErrorNotReady) fail(SPMV_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(query));
+      if (std::chrono::steady_clock::now() - start > std::chrono::milliseconds(timeout_ms)) {
+        comm->aborted = true;
+        fail(SPMV_ERR_TIMEOUT, "collectives did not complete in time; the communicator is aborted");
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+  });
+}
+
+int spmv_chain_run(const spmv_operator* shard_op, spmv_comm* comm, const int* shard_row_begin, void* x_current,
+                   void* x_next, int products, void* stream) {
+  return guarded([&] {
+    require(shard_op && comm && comm->comm && shard_row_begin && x_current && x_next && products >= 0, "bad arguments");
+    require(!comm->aborted, "the communicator was aborted");
+    spmv_operator_info info;
+    if (spmv_operator_get_info(shard_op, &info) != SPMV_OK) fail(SPMV_ERR_INVALID_ARGUMENT, "bad operator");
+    const int nranks = comm->nranks, rank = comm->rank;
+    const int64_t total_rows = shard_row_begin[nranks];
+    require(shard_row_begin[0] == 0 && shard_row_begin[rank + 1] - shard_row_begin[rank] == info.rows,
+            "the operator's rows do not match its shard");
+    require(info.cols == total_rows, "chained products need a square matrix (cols = total rows)");
+    const size_t value_bytes = (size_t)value_bytes_of(info.dtype);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    NcclApi& api = nccl();
+    char* current = static_cast<char*>(x_current);
+    char* next = static_cast<char*>(x_next);
+    for (int product = 0; product < products; ++product) {
+      // this rank's rows of y go straight into its slice of the next x
+      const int status = spmv_operator_run(shard_op, current, next + value_bytes * shard_row_begin[rank], stream);
+      if (status != SPMV_OK) fail(status, spmv_last_error());
+      nccl_check(api.group_start(), "ncclGroupStart");
+      for (int root = 0; root < nranks; ++root) {
+        const size_t count = (size_t)(shard_row_begin[root + 1] - shard_row_begin[root]);
+        if (count == 0) continue;
+        char* slice = next + value_bytes * shard_row_begin[root];
+        nccl_check(api.broadcast(slice, slice, count, nccl_type(info.dtype), root, comm->comm, s), "ncclBroadcast");
+      }
+      nccl_check(api.group_end(), "ncclGroupEnd");
+      std::swap(current, next);
+    }
+  });
+}
+
+}  // extern "C"

@@ -172,6 +172,11 @@ _sig("spmv_synth_block_fem", _i, _i, _i, _i, _i, _u64, _i, _i, _c_void_pp)
 _sig("spmv_fill_uniform", _i, _i, _i64, _u64, _v)
 _sig("spmv_fill_reference_x", _i, _i, _i64, _v)
 _sig("spmv_shard_rows", _i, _v, _i, _v)
+_sig("spmv_comm_unique_id", _i, _v)
+_sig("spmv_comm_create", _i, _i, _i, _v, _i, _c_void_pp)
+_sig("spmv_comm_destroy", None, _v)
+_sig("spmv_comm_check", _i, _v, _v, _i)
+_sig("spmv_chain_run", _i, _v, _v, _v, _v, _v, _i, _v)
 
 
 def _check(status: int):
@@ -552,6 +557,51 @@ class Operator:
 def launch(layout: int, dtype: int, tpr: int, device_matrix: DeviceMatrix, stream: int = 0):
     """launch<T> (bench_csr_width.cu:607) on caller-owned device arrays (no preprocessing)."""
     _check(_lib.spmv_launch(layout, dtype, tpr, ctypes.byref(device_matrix), stream or None))
+
+
+# ---------------------------------------------------------------------------------------------------
+# Multi-GPU: NCCL communicator and chained products over row shards
+# ---------------------------------------------------------------------------------------------------
+def comm_unique_id() -> bytes:
+    """The 128-byte NCCL id rank 0 creates and the other ranks receive (e.g. by torch.distributed)."""
+    buffer = ctypes.create_string_buffer(128)
+    _check(_lib.spmv_comm_unique_id(buffer))
+    return buffer.raw
+
+
+class Comm:
+    """An NCCL communicator of one rank (one process per GPU)."""
+
+    def __init__(self, nranks: int, rank: int, unique_id: bytes, device: int = -1):
+        handle = ctypes.c_void_p()
+        _check(_lib.spmv_comm_create(nranks, rank, ctypes.create_string_buffer(unique_id, 128), device,
+                                     ctypes.byref(handle)))
+        self._handle = handle
+        self.nranks, self.rank = nranks, rank
+
+    @property
+    def handle(self):
+        return self._handle
+
+    def check(self, stream: int = 0, timeout_ms: int = 30000):
+        _check(_lib.spmv_comm_check(self._handle, stream or None, timeout_ms))
+
+    def close(self):
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            _lib.spmv_comm_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        self.close()
+
+
+def chain_run(shard_op: "Operator", comm: Comm, shard_row_begin, x_current: int, x_next: int, products: int,
+              stream: int = 0):
+    """products chained y -> x: each rank's shard product into its slice of the next x, then the slices
+    all-gathered. The result is in x_current for an even count of products, in x_next for an odd one."""
+    bounds = np.ascontiguousarray(shard_row_begin, dtype=np.int32)
+    _check(_lib.spmv_chain_run(shard_op.handle, comm.handle, _pointer(bounds), x_current, x_next, products,
+                               stream or None))
 
 
 def exported_symbols() -> Sequence[str]:

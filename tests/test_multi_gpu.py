@@ -1,0 +1,61 @@
+"""Chained products over NCCL on two GPUs (spmv_chain_run): each rank's CSR-lp shard product into its
+slice of the next x, the slices all-gathered, three times; the result bit-identical to the oracle's
+chain on the whole matrix."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def free_port():
+    with socket.socket() as probe:
+        probe.bind(("127.0.0.1", 0))
+        return probe.getsockname()[1]
+
+
+def worker(rank, world, port):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "spmv-index-compression_b200"))
+    sys.path.insert(0, os.path.join(root, "oracle"))
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import oracle
+    import spmvb200 as spmv
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    box = [spmv.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    comm = spmv.Comm(world, rank, box[0], device=rank)
+    matrix = spmv.synth_random_band(20000, 500, 12.0, 3)
+    bounds = spmv.shard_rows(matrix, world)
+    shard = matrix.slice_rows(int(bounds[rank]), int(bounds[rank + 1]))
+    x0 = spmv.fill_uniform(spmv.F64, matrix.cols, 9)
+    with spmv.Operator(shard, spmv.LP, spmv.F64, 8, device=rank) as op:
+        x_current = torch.from_numpy(x0).cuda()
+        x_next = torch.zeros_like(x_current)
+        stream = torch.cuda.current_stream().cuda_stream
+        spmv.chain_run(op, comm, bounds, x_current.data_ptr(), x_next.data_ptr(), 3, stream)
+        comm.check(stream, 30000)
+        result = x_next.cpu().numpy()    # an odd count of products ends in x_next
+    row_ptr, col_ind, values = matrix.arrays()
+    expected = x0.copy()
+    for _ in range(3):
+        expected = oracle.spmv_csr(row_ptr, col_ind, values, expected, spmv.F64, spmv.LP, 8)
+    comm.close()
+    dist.destroy_process_group()
+    assert np.array_equal(result.view(np.uint64), expected.view(np.uint64))
+
+
+def test_chained_products_over_nccl():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(worker, args=(2, free_port()), nprocs=2, join=True)
