@@ -181,9 +181,11 @@ typedef struct {
   int value_rounding;     /* 0: values (T)(float)val as upload_matrix does (:927); 1: (T)val          */
   int device;             /* CUDA device ordinal (-1 = current device)                               */
   int stages;             /* shared-memory tile buffers per CTA, 1..4 (0 = default)                  */
+  int tile_rows;          /* rows a tile holds at most, a multiple of 16 (0 = chosen by the library)  */
 } spmv_operator_config;
 
-/* Fills a config with defaults: physical_tpr 0, tile_nnz 0, value_rounding 0, device -1, stages 0. */
+/* Fills a config with defaults: physical_tpr 0, tile_nnz 0, value_rounding 0, device -1, stages 0,
+ * tile_rows 0. */
 void spmv_operator_config_init(spmv_operator_config* config, int layout, int dtype, int tpr);
 
 /* upload_matrix + upload_* (bench_csr_width.cu:795-951): encodes the matrix in the layout, converts

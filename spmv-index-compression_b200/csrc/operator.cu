@@ -106,14 +106,14 @@ TilePlan plan_tiles(const Csr& matrix, int tile_nnz, int tile_rows, const int* r
   return plan;
 }
 
-// Physical threads per row P: as many as leave every row of a typical tile a group of its own (the
-// 256/P groups of a CTA take one row each per pass), and at least T/16 (at most 16 lane sums per
-// thread; T/8 for CSR-lp, whose 16-lane variants gather half as deep). Measured on B200 with
-// 4096-nonzero tiles: P = 1 for 27-entry rows at T = 8, P = 2 for 33-entry rows, P = 4 for CSR-lp at
-// T = 32.
-int choose_physical_tpr(int tpr, int layout, double rows_per_tile) {
+// Physical threads per row P: the fewest that leave a thread at most 32 entries of an average row (one
+// batch of gathers), and at least T/16 (at most 16 lane sums per thread; T/8 for CSR-lp, whose 16-lane
+// variants gather half as deep). A tile then holds 256/P rows (at least 128), so that one pass of the
+// CTA's 256/P row groups covers it. Measured on B200 (27-point stencil, FP64): P = 1 at T = 8 and P = 2
+// with 128-row tiles at T = 32 both reach about 82 % of the measured HBM peak in CSR-i32.
+int choose_physical_tpr(int tpr, int layout, double mean_length) {
   int physical = 1;
-  while (physical * 2 <= tpr && (double)(kTileBlock / (physical * 2)) >= rows_per_tile) physical *= 2;
+  while (physical < tpr && mean_length / physical > 32.0) physical *= 2;
   const int max_slots = layout == SPMV_LAYOUT_LP ? 8 : 16;
   while (tpr / physical > max_slots) physical *= 2;
   return physical;
@@ -239,11 +239,11 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     op->cols = m.cols;
     op->nnz = m.nnz();
     op->memory = memory_of(m, facts, layout, dtype, tpr);
-    op->tile_nnz = config->tile_nnz > 0 ? config->tile_nnz : 4096;
-    // rows of a tile at most: twice the rows of an average tile, so short-row tiles still fill up
     const double mean_length = m.rows > 0 ? (double)m.nnz() / m.rows : 1.0;
-    op->tile_rows = std::max(64, std::min(std::max(64, op->tile_nnz), (int)(2.0 * op->tile_nnz / std::max(mean_length, 1.0)) + 16));
-    op->tile_rows = (op->tile_rows + 15) & ~15;
+    op->physical_tpr = config->physical_tpr > 0 ? config->physical_tpr : choose_physical_tpr(tpr, layout, mean_length);
+    op->tile_rows = config->tile_rows > 0 ? config->tile_rows : std::max(128, kTileBlock / op->physical_tpr);
+    require(op->tile_rows % 16 == 0 && op->tile_rows <= 16384, "tile_rows must be a multiple of 16, at most 16384");
+    op->tile_nnz = config->tile_nnz > 0 ? config->tile_nnz : 4096;
     op->stages = config->stages > 0 ? config->stages : 2;
     require(op->stages >= 1 && op->stages <= kMaxStages, "stages must be 0 or 1..4");
     int shared_limit = 0, multiprocessors = 0;
@@ -255,13 +255,8 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
       int per_sm = 0;
       cuda_check(cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, op->device), "device attribute");
       const int budget = per_sm / 2 - 1024 - 1024;   // per CTA: minus the reserved and static shared memory
-      auto rows_for = [&](int tile_nnz) {
-        const int rows = std::max(64, std::min(std::max(64, tile_nnz), (int)(2.0 * tile_nnz / std::max(mean_length, 1.0)) + 16));
-        return (rows + 15) & ~15;
-      };
-      while (op->tile_nnz > 256 && tile_smem_bytes(op->tile_nnz, rows_for(op->tile_nnz), value_bytes, layout, op->stages) > budget)
+      while (op->tile_nnz > 256 && tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages) > budget)
         op->tile_nnz -= 256;
-      op->tile_rows = rows_for(op->tile_nnz);
     }
     const int smem = tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages);
     if (smem > shared_limit)
@@ -323,9 +318,6 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     op->long_rows = device_upload<int>(plan.long_rows.data(), plan.long_rows.size(), op->device_bytes);
     op->status = device_upload<unsigned>(nullptr, 1, op->device_bytes);
     cuda_check(cudaMemset(op->status, 0, sizeof(unsigned)), "cudaMemset");
-    const double mean = plan.short_rows > 0 ? (double)plan.short_nnz / (double)plan.short_rows : 1.0;
-    const double rows_per_tile = std::min<double>(op->tile_rows, op->tile_nnz / std::max(mean, 1.0));
-    op->physical_tpr = config->physical_tpr > 0 ? config->physical_tpr : choose_physical_tpr(tpr, layout, rows_per_tile);
     // long rows: one CTA per row at a time; a chunk of a long row (values, gathered x and, for CSR-lp,
     // decoded columns) lives in the CTA's shared memory, at least kTileBlock entries, at most 8192, and
     // the launch gets the larger of the tile buffers and one chunk

@@ -89,7 +89,7 @@ class MemoryBreakdown(ctypes.Structure):
 class OperatorConfig(ctypes.Structure):
     _fields_ = [("layout", ctypes.c_int), ("dtype", ctypes.c_int), ("tpr", ctypes.c_int),
                 ("physical_tpr", ctypes.c_int), ("tile_nnz", ctypes.c_int), ("value_rounding", ctypes.c_int),
-                ("device", ctypes.c_int), ("stages", ctypes.c_int)]
+                ("device", ctypes.c_int), ("stages", ctypes.c_int), ("tile_rows", ctypes.c_int)]
 
 
 class OperatorInfo(ctypes.Structure):
@@ -495,7 +495,7 @@ class Operator:
     """A matrix encoded in one layout and uploaded to a GPU; run() is launch<T> at the operator's T."""
 
     def __init__(self, matrix: CsrMatrix, layout: int, dtype: int, tpr: int, physical_tpr: int = 0,
-                 tile_nnz: int = 0, value_rounding: int = 0, device: int = -1, stages: int = 0):
+                 tile_nnz: int = 0, value_rounding: int = 0, device: int = -1, stages: int = 0, tile_rows: int = 0):
         config = OperatorConfig()
         _lib.spmv_operator_config_init(ctypes.byref(config), layout, dtype, tpr)
         config.physical_tpr = physical_tpr
@@ -503,6 +503,7 @@ class Operator:
         config.value_rounding = value_rounding
         config.device = device
         config.stages = stages
+        config.tile_rows = tile_rows
         handle = ctypes.c_void_p()
         _check(_lib.spmv_operator_create(matrix.handle, ctypes.byref(config), ctypes.byref(handle)))
         self._handle = handle
