@@ -255,6 +255,11 @@ typedef struct {
  * preprocessing and no workspace. */
 int spmv_launch(int layout, int dtype, int tpr, const spmv_device_matrix* matrix, void* stream);
 
+/* measure_read_bandwidth (include/roofline.cuh:101): the median bandwidth of a pure streaming read of a
+ * `bytes`-byte device buffer (16-byte vector loads, no reuse), over `reps` timed passes after 3 warm-ups,
+ * on the current device. The roof of the reference's epsilon. */
+int spmv_read_bandwidth(int64_t bytes, int reps, double* gigabytes_per_second);
+
 /* ---- synthetic matrices for the benchmark configurations ---------------------------------------- */
 /* 2D 5-point Laplacian on grid x grid (diagonal 4, neighbours -1). */
 int spmv_synth_laplacian2d(int grid, spmv_csr** out);

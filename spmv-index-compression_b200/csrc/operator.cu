@@ -455,3 +455,65 @@ int spmv_launch(int layout, int dtype, int tpr, const spmv_device_matrix* matrix
 }
 
 }  // extern "C"
+
+// ---- measured read bandwidth (the roof of the reference's epsilon, roofline.cuh:101) --------------------
+namespace spmvb200 {
+namespace {
+
+// Every thread streams 16-byte vectors of the buffer with no reuse; the reduction result is kept only to
+// stop the loads being dropped.
+__global__ void __launch_bounds__(512) k_read_stream(const uint4* __restrict__ source, size_t vectors, unsigned* sink) {
+  unsigned accumulator = 0;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t index = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+#pragma unroll 4
+  for (; index < vectors; index += stride) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(source + index));
+    accumulator ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (accumulator == 0x9e3779b9u) *sink = accumulator;   // practically never: keeps the loads alive
+}
+
+}  // namespace
+}  // namespace spmvb200
+
+extern "C" int spmv_read_bandwidth(int64_t bytes, int reps, double* gigabytes_per_second) {
+  return guarded([&] {
+    require(gigabytes_per_second && reps >= 1 && bytes >= (1 << 20), "bad arguments");
+    const size_t vectors = (size_t)bytes / sizeof(uint4);
+    uint4* buffer = nullptr;
+    unsigned* sink = nullptr;
+    cuda_check(cudaMalloc(&buffer, vectors * sizeof(uint4)), "cudaMalloc");
+    cudaError_t status = cudaMalloc(&sink, sizeof(unsigned));
+    if (status == cudaSuccess) status = cudaMemset(buffer, 1, vectors * sizeof(uint4));
+    int multiprocessors = 0, device = 0;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
+    const unsigned blocks = (unsigned)multiprocessors * 4;
+    cudaEvent_t start = nullptr, end = nullptr;
+    std::vector<float> times;
+    if (status == cudaSuccess) status = cudaEventCreate(&start);
+    if (status == cudaSuccess) status = cudaEventCreate(&end);
+    for (int rep = -3; rep < reps && status == cudaSuccess; ++rep) {
+      cudaEventRecord(start);
+      k_read_stream<<<blocks, 512>>>(buffer, vectors, sink);
+      cudaEventRecord(end);
+      status = cudaGetLastError();
+      if (status == cudaSuccess) status = cudaEventSynchronize(end);
+      float ms = 0.0f;
+      if (status == cudaSuccess) status = cudaEventElapsedTime(&ms, start, end);
+      if (rep >= 0) times.push_back(ms);
+    }
+    if (start) cudaEventDestroy(start);
+    if (end) cudaEventDestroy(end);
+    cudaFree(buffer);
+    if (sink) cudaFree(sink);
+    cuda_check(status, "read bandwidth");
+    std::sort(times.begin(), times.end());
+    const double median = times[times.size() / 2];
+    *gigabytes_per_second = (double)(vectors * sizeof(uint4)) / (median * 1e-3) / 1e9;
+  });
+}

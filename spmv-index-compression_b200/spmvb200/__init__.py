@@ -172,6 +172,7 @@ _sig("spmv_synth_block_fem", _i, _i, _i, _i, _i, _u64, _i, _i, _c_void_pp)
 _sig("spmv_fill_uniform", _i, _i, _i64, _u64, _v)
 _sig("spmv_fill_reference_x", _i, _i, _i64, _v)
 _sig("spmv_shard_rows", _i, _v, _i, _v)
+_sig("spmv_read_bandwidth", _i, _i64, _i, ctypes.POINTER(_d))
 _sig("spmv_comm_unique_id", _i, _v)
 _sig("spmv_comm_create", _i, _i, _i, _v, _i, _c_void_pp)
 _sig("spmv_comm_destroy", None, _v)
@@ -553,6 +554,14 @@ class Operator:
     def check(self):
         """Raises SpmvError(ERR_TIMEOUT) if a bounded device-side wait gave up since the last check."""
         _check(_lib.spmv_operator_check(self._handle))
+
+
+def read_bandwidth(bytes_: int = 4 << 30, reps: int = 20) -> float:
+    """Measured streaming read bandwidth of the current device in GB/s (measure_read_bandwidth,
+    roofline.cuh:101)."""
+    result = ctypes.c_double()
+    _check(_lib.spmv_read_bandwidth(bytes_, reps, ctypes.byref(result)))
+    return result.value
 
 
 def launch(layout: int, dtype: int, tpr: int, device_matrix: DeviceMatrix, stream: int = 0):

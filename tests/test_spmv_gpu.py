@@ -245,3 +245,12 @@ def test_laplacian_config_bit_identical():
     for layout in (spmv.I32, spmv.I16, spmv.R16):
         with spmv.Operator(matrix, layout, spmv.F64, 4) as op:
             assert np.array_equal(bits(device_run(op, x)), bits(expected))
+
+
+def test_read_bandwidth_is_a_device_memory_rate():
+    """The read roof behind epsilon: a streaming read of 1 GiB (past the 126 MB L2), between 1 TB/s and the
+    nominal 8 TB/s of HBM3e on this device."""
+    rate = spmv.read_bandwidth(1 << 30, 5)
+    assert 1000.0 < rate < 8200.0
+    with pytest.raises(spmv.SpmvError):
+        spmv.read_bandwidth(0, 5)
