@@ -182,10 +182,16 @@ typedef struct {
   int device;             /* CUDA device ordinal (-1 = current device)                               */
   int stages;             /* shared-memory tile buffers per CTA, 1..4 (0 = default)                  */
   int tile_rows;          /* rows a tile holds at most, a multiple of 16 (0 = chosen by the library)  */
+  int schedule;           /* SPMV_SCHEDULE_*: how rows are mapped to the kernel (0 = chosen by the library) */
 } spmv_operator_config;
 
+/* Row schedules. Tiles: runs of consecutive rows staged in shared memory (rows of similar lengths).
+ * Classes: rows grouped by length, each group on its own thread mapping straight from global memory
+ * (skewed row lengths, such as power-law graphs). Both give the same results. */
+enum { SPMV_SCHEDULE_AUTO = 0, SPMV_SCHEDULE_TILES = 1, SPMV_SCHEDULE_CLASSES = 2 };
+
 /* Fills a config with defaults: physical_tpr 0, tile_nnz 0, value_rounding 0, device -1, stages 0,
- * tile_rows 0. */
+ * tile_rows 0, schedule SPMV_SCHEDULE_AUTO. */
 void spmv_operator_config_init(spmv_operator_config* config, int layout, int dtype, int tpr);
 
 /* upload_matrix + upload_* (bench_csr_width.cu:795-951): encodes the matrix in the layout, converts
@@ -209,6 +215,9 @@ typedef struct {
   int64_t long_rows;         /* rows longer than a tile, streamed by the long-row path       */
   int64_t device_bytes;      /* bytes of device memory the operator holds                    */
   spmv_memory memory;        /* memory_of of this layout at this T (algorithmic bytes/product) */
+  int schedule;              /* SPMV_SCHEDULE_TILES or SPMV_SCHEDULE_CLASSES                 */
+  int64_t listed_rows;       /* classes: rows of more than 8 entries on groups of P threads  */
+  int64_t blocks;            /* CTAs of one launch                                           */
 } spmv_operator_info;
 int spmv_operator_get_info(const spmv_operator* op, spmv_operator_info* info);
 

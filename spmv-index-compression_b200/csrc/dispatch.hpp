@@ -28,6 +28,31 @@ cudaError_t launch_vector_f64(int layout, int tpr, const KernelArgs& a, int64_t 
 cudaError_t launch_vector_f32(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream);
 cudaError_t launch_vector_f16(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream);
 
+// k_spmv_classes over `blocks` CTAs of kTileBlock threads with `smem` bytes of dynamic shared memory; the
+// prepare functions raise the kernel's shared-memory limit to smem.
+cudaError_t launch_classes_f64(int layout, int tpr, const KernelArgs& a, int64_t blocks, int smem, cudaStream_t stream);
+cudaError_t launch_classes_f32(int layout, int tpr, const KernelArgs& a, int64_t blocks, int smem, cudaStream_t stream);
+cudaError_t launch_classes_f16(int layout, int tpr, const KernelArgs& a, int64_t blocks, int smem, cudaStream_t stream);
+cudaError_t prepare_classes_f64(int layout, int tpr, int smem);
+cudaError_t prepare_classes_f32(int layout, int tpr, int smem);
+cudaError_t prepare_classes_f16(int layout, int tpr, int smem);
+
+inline cudaError_t launch_classes(int dtype, int layout, int tpr, const KernelArgs& a, int64_t blocks, int smem, cudaStream_t stream) {
+  switch (dtype) {
+    case SPMV_F64: return launch_classes_f64(layout, tpr, a, blocks, smem, stream);
+    case SPMV_F32: return launch_classes_f32(layout, tpr, a, blocks, smem, stream);
+    default:       return launch_classes_f16(layout, tpr, a, blocks, smem, stream);
+  }
+}
+
+inline cudaError_t prepare_classes(int dtype, int layout, int tpr, int smem) {
+  switch (dtype) {
+    case SPMV_F64: return prepare_classes_f64(layout, tpr, smem);
+    case SPMV_F32: return prepare_classes_f32(layout, tpr, smem);
+    default:       return prepare_classes_f16(layout, tpr, smem);
+  }
+}
+
 inline cudaError_t launch_tiles(int dtype, int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream) {
   switch (dtype) {
     case SPMV_F64: return launch_tiles_f64(layout, tpr, physical_tpr, a, stream);

@@ -103,6 +103,13 @@ struct KernelArgs {
   int smem_bytes;            // k_spmv_tiles: dynamic shared memory of the launch
   int64_t tile_ctas;         // k_spmv_tiles: persistent CTAs over the tiles after the vector blocks
   unsigned* status;          // device status word (may be null)
+  // k_spmv_classes (rows by length): long-row blocks, then the blocks of each segment of listed rows
+  // (P = 32, 16, ..., 1 threads per row), then the short-row blocks
+  const int4* row_items;     // {row, first entry, end entry, row base} of the listed rows, by segment
+  int64_t long_blocks;       // one CTA per row of row_list
+  int64_t segment_first[6];  // segment s (P = 2^s): its first item,
+  int64_t segment_items[6];  // its items
+  int64_t segment_blocks[6]; // and its blocks of 256 / P items
 };
 
 // ---- shared-memory plan of a tile CTA (host and device compute it alike) ----------------------------
@@ -301,58 +308,155 @@ __device__ __forceinline__ void vector_rows(const KernelArgs& a, int64_t block, 
   }
 }
 
-// ---- a resident tile, from one shared-memory buffer -------------------------------------------------
-// Rows go to groups of P threads in passes; every thread runs every pass, so the shuffles of the
-// reduction always see the full warp. A thread gathers x for up to kGathers of its entries at once (R
-// rounds of its S lanes) into registers, then adds them into its lane chains in order, reading the values
-// from shared memory; a row of up to R*T entries costs one round trip to memory.
-#ifndef SPMV_TILE_GATHERS
-#define SPMV_TILE_GATHERS 32
-#endif
-constexpr int kGathers = SPMV_TILE_GATHERS;
-
-// The stage's images, shifted so that they are indexed by absolute row, entry or word.
+// ---- rows on groups of P threads ----------------------------------------------------------------------
+// Where a row's data is read from: the shifted images of a resident tile in shared memory, or the
+// operator's arrays in global memory (read-only path). Both are indexed by absolute row, entry and word.
 template <class V, int LAYOUT>
 struct TileView {
   using Index = typename LayoutTraits<LAYOUT>::Index;
   int row_begin, rows;
-  const int* row_ptr;
-  const int* row_base;
-  const int* row_word;
-  const uint8_t* row_width;
-  const V* values;
-  const Index* index;
+  const int* row_ptr_;
+  const int* row_base_;
+  const int* row_word_;
+  const uint8_t* row_width_;
+  const V* values_;
+  const Index* index_;
   __device__ __forceinline__ TileView(const unsigned char* stage, const StagePlan& plan) {
     const int* header = reinterpret_cast<const int*>(stage + plan.header);
     row_begin = header[0];
     rows = header[1];
-    row_ptr = reinterpret_cast<const int*>(stage + plan.row_ptr) - header[2];
-    row_base = reinterpret_cast<const int*>(stage + plan.row_base) - header[3];
-    row_word = reinterpret_cast<const int*>(stage + plan.row_word) - header[3];
-    row_width = reinterpret_cast<const uint8_t*>(stage + plan.row_width) - header[4];
-    values = reinterpret_cast<const V*>(stage + plan.values) - header[5];
-    index = reinterpret_cast<const Index*>(stage + plan.index) - header[6];
+    row_ptr_ = reinterpret_cast<const int*>(stage + plan.row_ptr) - header[2];
+    row_base_ = reinterpret_cast<const int*>(stage + plan.row_base) - header[3];
+    row_word_ = reinterpret_cast<const int*>(stage + plan.row_word) - header[3];
+    row_width_ = reinterpret_cast<const uint8_t*>(stage + plan.row_width) - header[4];
+    values_ = reinterpret_cast<const V*>(stage + plan.values) - header[5];
+    index_ = reinterpret_cast<const Index*>(stage + plan.index) - header[6];
   }
+  __device__ __forceinline__ int row_ptr(int row) const { return row_ptr_[row]; }
+  __device__ __forceinline__ int row_base(int row) const { return row_base_[row]; }
+  __device__ __forceinline__ int row_word(int row) const { return row_word_[row]; }
+  __device__ __forceinline__ uint32_t row_width(int row) const { return row_width_[row]; }
+  __device__ __forceinline__ V value(int entry) const { return values_[entry]; }
+  __device__ __forceinline__ Index index(int entry) const { return index_[entry]; }
+  __device__ __forceinline__ uint32_t word(int64_t w) const { return reinterpret_cast<const uint32_t*>(index_)[w]; }
 };
 
-// Delta k of a CSR-lp lane whose run starts at bit `start` of the row's stream (bit width * (lane *
-// quotient + min(lane, remainder)), lane_major_bit of the reference): bits [start + k*width, +width) of
-// the tile's words, which the two 32-bit words around it always hold (a width never exceeds 32 bits).
-__device__ __forceinline__ uint32_t packed_delta(const uint32_t* words, uint32_t bit, uint32_t mask) {
-  return __funnelshift_r(words[bit >> 5], words[(bit >> 5) + 1], bit & 31) & mask;
+template <class V, int LAYOUT>
+struct GlobalView {
+  using Index = typename LayoutTraits<LAYOUT>::Index;
+  const KernelArgs& a;
+  __device__ __forceinline__ explicit GlobalView(const KernelArgs& args) : a(args) {}
+  __device__ __forceinline__ int row_ptr(int row) const { return load_readonly(a.row_ptr + row); }
+  __device__ __forceinline__ int row_base(int row) const { return load_readonly(a.row_base + row); }
+  __device__ __forceinline__ int row_word(int row) const { return load_readonly(a.row_word + row); }
+  __device__ __forceinline__ uint32_t row_width(int row) const { return load_readonly(a.row_width + row); }
+  __device__ __forceinline__ V value(int entry) const { return load_readonly(static_cast<const V*>(a.values) + entry); }
+  __device__ __forceinline__ Index index(int entry) const { return load_readonly(static_cast<const Index*>(a.columns) + entry); }
+  __device__ __forceinline__ uint32_t word(int64_t w) const { return load_readonly(a.words + w); }
+};
+
+// Delta of a CSR-lp lane at bit `bit` of the row's stream starting at word w0 (bit width * (lane *
+// quotient + min(lane, remainder) + k) for its k-th delta, lane_major_bit of the reference): the two
+// 32-bit words around it always hold it (a width never exceeds 32 bits).
+template <class View>
+__device__ __forceinline__ uint32_t packed_delta(const View& view, int64_t w0, uint32_t bit, uint32_t mask) {
+  const int64_t w = w0 + (bit >> 5);
+  return __funnelshift_r(view.word(w), view.word(w + 1), bit & 31) & mask;
 }
 
-template <class V, int LAYOUT, int T, int P>
-__device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned char* stage, const StagePlan& plan) {
+// The product of one row (entries [entry_begin, entry_end), column base `base` for the row-relative and
+// CSR-lp layouts) on its P threads (thread p of the group): the lane sums of the logical lanes p, p+P, ...
+// and the reduction tree. Every thread of the warp must call it (the tree shuffles); rows of
+// inactive groups contribute nothing. A thread gathers x for up to kBatch of its entries at once (R rounds
+// of its S lanes) into registers, then adds them into its lane chains in order.
+template <class V, int LAYOUT, int T, int P, int kBatch, class View>
+__device__ __forceinline__ typename ValueTraits<V>::Acc row_product(const View& view, const V* __restrict__ x, int row,
+                                                                    int entry_begin, int entry_end, int base, bool active,
+                                                                    int p) {
   using VT = ValueTraits<V>;
   using Acc = typename VT::Acc;
   constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
   constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
   constexpr int S = T / P;
+  constexpr int R = S >= kBatch ? 1 : kBatch / S;
+  Acc acc[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) acc[j] = Acc(0);
+  if (active) {
+    if constexpr (!kPacked) {
+      if constexpr (!kBase) base = 0;   // absolute columns
+      for (int entry = entry_begin + p; entry < entry_end; entry += T * R) {
+        V xv[R][S];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int j = 0; j < S; ++j) {
+            const int e = entry + r * T + j * P;
+            if (e < entry_end) xv[r][j] = load_readonly(x + base + (int)view.index(e));
+          }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int j = 0; j < S; ++j) {
+            const int e = entry + r * T + j * P;
+            if (e < entry_end) acc[j] = VT::fma(VT::widen(view.value(e)), VT::widen(xv[r][j]), acc[j]);
+          }
+      }
+    } else {
+      // lane p + j*P owns quotient (+1 below remainder) deltas from bit width * (lane * quotient +
+      // min(lane, remainder)); both are recomputed where used, so only the running columns stay live
+      const int length = entry_end - entry_begin;
+      const int quotient = length / T, remainder = length - quotient * T;
+      const uint32_t width = view.row_width(row);
+      const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
+      const int64_t w0 = view.row_word(row);
+      int column[S];
+#pragma unroll
+      for (int j = 0; j < S; ++j) column[j] = base;
+      const int rounds = quotient + (remainder > 0 ? 1 : 0);
+      for (int round = 0; round < rounds; round += R) {
+        V xv[R][S];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int j = 0; j < S; ++j) {
+            const int lane = p + j * P;
+            if (round + r < quotient + (lane < remainder ? 1 : 0)) {
+              const uint32_t delta = (uint32_t)(lane * quotient + (lane < remainder ? lane : remainder) + round + r);
+              column[j] += (int)packed_delta(view, w0, delta * width, mask);
+              xv[r][j] = load_readonly(x + column[j]);
+            }
+          }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int j = 0; j < S; ++j) {
+            const int lane = p + j * P;
+            if (round + r < quotient + (lane < remainder ? 1 : 0))
+              acc[j] = VT::fma(VT::widen(view.value(entry_begin + lane + (round + r) * T)), VT::widen(xv[r][j]), acc[j]);
+          }
+      }
+    }
+  }
+  return reduce_lanes<VT, Acc, T, P>(acc);
+}
+
+// ---- a resident tile, from one shared-memory buffer -------------------------------------------------
+// Rows go to groups of P threads in passes; every thread runs every pass, so the shuffles of the
+// reduction always see the full warp; a row of up to R*T entries costs one round trip to memory.
+#ifndef SPMV_TILE_GATHERS
+#define SPMV_TILE_GATHERS 32
+#endif
+constexpr int kGathers = SPMV_TILE_GATHERS;
+
+template <class V, int LAYOUT, int T, int P>
+__device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned char* stage, const StagePlan& plan) {
+  using VT = ValueTraits<V>;
+  constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
+  constexpr int S = T / P;
   // x values gathered at once per thread: 32, or 16 for FP64 when 16 lane sums (or 8 CSR-lp lanes with
   // their running columns) already hold many of the 128 registers two CTAs of 256 threads leave a thread
   constexpr int kBatch = (sizeof(V) == 8 && (S >= 16 || (kPacked && S >= 8))) ? kGathers / 2 : kGathers;
-  constexpr int R = S >= kBatch ? 1 : kBatch / S;
   constexpr int kGroups = kTileBlock / P;
   const TileView<V, LAYOUT> tile(stage, plan);
   const V* x = static_cast<const V*>(a.x);
@@ -362,68 +466,11 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
   for (int first = 0; first < tile.rows; first += kGroups) {
     const int local = first + group;
     const int row = tile.row_begin + local;
-    Acc acc[S];
-#pragma unroll
-    for (int j = 0; j < S; ++j) acc[j] = Acc(0);
-    if (local < tile.rows) {
-      const int entry_begin = tile.row_ptr[row], entry_end = tile.row_ptr[row + 1];
-      if constexpr (!kPacked) {
-        const int base = kBase ? tile.row_base[row] : 0;
-        for (int entry = entry_begin + p; entry < entry_end; entry += T * R) {
-          V xv[R][S];
-#pragma unroll
-          for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int j = 0; j < S; ++j) {
-              const int e = entry + r * T + j * P;
-              if (e < entry_end) xv[r][j] = load_readonly(x + base + (int)tile.index[e]);
-            }
-#pragma unroll
-          for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int j = 0; j < S; ++j) {
-              const int e = entry + r * T + j * P;
-              if (e < entry_end) acc[j] = VT::fma(VT::widen(tile.values[e]), VT::widen(xv[r][j]), acc[j]);
-            }
-        }
-      } else {
-        // lane p + j*P owns quotient (+1 below remainder) deltas from bit width * (lane * quotient +
-        // min(lane, remainder)); both are recomputed where used, so only the running columns stay live
-        const int length = entry_end - entry_begin;
-        const int quotient = length / T, remainder = length - quotient * T;
-        const uint32_t width = tile.row_width[row];
-        const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
-        const uint32_t* words = reinterpret_cast<const uint32_t*>(tile.index) + tile.row_word[row];
-        int column[S];
-#pragma unroll
-        for (int j = 0; j < S; ++j) column[j] = tile.row_base[row];
-        const int rounds = quotient + (remainder > 0 ? 1 : 0);
-        for (int round = 0; round < rounds; round += R) {
-          V xv[R][S];
-#pragma unroll
-          for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int j = 0; j < S; ++j) {
-              const int lane = p + j * P;
-              if (round + r < quotient + (lane < remainder ? 1 : 0)) {
-                const uint32_t delta = (uint32_t)(lane * quotient + (lane < remainder ? lane : remainder) + round + r);
-                column[j] += (int)packed_delta(words, delta * width, mask);
-                xv[r][j] = load_readonly(x + column[j]);
-              }
-            }
-#pragma unroll
-          for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int j = 0; j < S; ++j) {
-              const int lane = p + j * P;
-              if (round + r < quotient + (lane < remainder ? 1 : 0))
-                acc[j] = VT::fma(VT::widen(tile.values[entry_begin + lane + (round + r) * T]), VT::widen(xv[r][j]), acc[j]);
-            }
-        }
-      }
-    }
-    const Acc sum = reduce_lanes<VT, Acc, T, P>(acc);
-    if (p == 0 && local < tile.rows) y[row] = VT::narrow(sum);
+    const bool active = local < tile.rows;
+    const int begin = active ? tile.row_ptr(row) : 0, end = active ? tile.row_ptr(row + 1) : 0;
+    const int base = active && LayoutTraits<LAYOUT>::kBase ? tile.row_base(row) : 0;
+    const auto sum = row_product<V, LAYOUT, T, P, kBatch>(tile, x, row, begin, end, base, active, p);
+    if (p == 0 && active) y[row] = VT::narrow(sum);
   }
 }
 
@@ -478,10 +525,26 @@ __device__ __forceinline__ void issue_tile(const KernelArgs& a, int64_t tile_id,
 
 // ---- rows longer than a tile ----------------------------------------------------------------------------
 // A row of the long-row list takes a whole CTA, chunk by chunk (a chunk starts at a multiple of T within
-// the row, so an entry keeps its lane). Per chunk: for CSR-lp, the T lane owners decode their chains'
-// columns into shared memory; then all threads load the chunk's values and gather x at its columns into
-// shared memory, every load independent of the others; then the T lane owners add the chunk into their
-// lane sums in order. The lane sums finish in the width-T shuffle tree of warp 0.
+// the row, so an entry keeps its lane), with the warps specialised: warps 1..7 produce, warp 0 consumes.
+// Producers fill one of two shared-memory buffers per chunk with the chunk's values and x gathered at
+// its columns (CSR-lp: first the T lane owners among them decode their lanes' columns for the chunk);
+// the consumer's T lane owners add the chunk into their lane sums in order, while the producers fill the
+// other buffer. Named barriers hand the buffers over: 1 + b "buffer b full", 3 + b "buffer b free", 5 the
+// producers' decode. Every thread walks the same rows and chunks, so every barrier completes. The lane
+// sums finish in the width-T shuffle tree of warp 0.
+constexpr int kLongProducers = kTileBlock - 32;
+
+__host__ __device__ inline int long_smem_bytes(int chunk, int value_bytes, bool packed) {
+  return 4 * chunk * value_bytes + (packed ? 8 * chunk : 0);
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_barrier_arrive(int id, int threads) {
+  asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 template <class V, int LAYOUT, int T>
 __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* smem, int64_t block, int64_t blocks) {
   using VT = ValueTraits<V>;
@@ -490,62 +553,220 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
   constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
   constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
   const int chunk = a.long_chunk;   // entries per chunk: a multiple of kTileBlock (and so of T)
-  if ((int64_t)chunk * (2 * (int)sizeof(V) + 4) > a.smem_bytes) {   // never by construction
+  if (long_smem_bytes(chunk, (int)sizeof(V), kPacked) > a.smem_bytes) {   // never by construction
     if (threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusSmem);
     return;
   }
-  V* s_values = reinterpret_cast<V*>(smem);
-  V* s_x = s_values + chunk;
-  int* s_columns = reinterpret_cast<int*>(s_x + chunk);
+  V* const s_values = reinterpret_cast<V*>(smem);            // [2][chunk]
+  V* const s_x = s_values + 2 * chunk;                        // [2][chunk]
+  int* const s_columns = reinterpret_cast<int*>(s_x + 2 * chunk);   // CSR-lp: [2][chunk]
   const V* values = static_cast<const V*>(a.values);
   const V* x = static_cast<const V*>(a.x);
   const Index* index = static_cast<const Index*>(a.columns);
-  V* y = static_cast<V*>(a.y);
-  const int lane = threadIdx.x;   // lane owner when < T
+  const bool consumer = threadIdx.x < 32;
+  const int lane = threadIdx.x;                 // consumer: lane owner when < T
+  const int producer = (int)threadIdx.x - 32;   // producers: 0..kLongProducers-1, lane owner when < T
 
   for (int64_t item = block; item < a.row_count; item += blocks) {
     const int row = a.row_list[item];
     const int64_t begin = a.row_ptr[row], length = a.row_ptr[row + 1] - begin;
-    const int base = kBase ? a.row_base[row] : 0;
-    Acc sum = Acc(0);
-    // CSR-lp lane state (owners only): the next delta's bit and the running column
-    const int quotient = (int)(length / T), remainder = (int)(length - (int64_t)quotient * T);
-    const uint32_t width = kPacked ? a.row_width[row] : 0u;
-    const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
-    const uint32_t* words = kPacked ? a.words + a.row_word[row] : nullptr;
-    uint64_t bit = kPacked && lane < T ? (uint64_t)width * (uint64_t)(lane * quotient + (lane < remainder ? lane : remainder)) : 0;
-    int column = base;
-
-    for (int64_t first = 0; first < length; first += chunk) {
-      const int count = (int)(length - first < chunk ? length - first : chunk);
-      if constexpr (kPacked) {
+    const int chunks = (int)((length + chunk - 1) / chunk);
+    if (consumer) {
+      Acc sum = Acc(0);
+      for (int k = 0; k < chunks; ++k) {
+        const int b = k & 1;
+        const int count = (int)(length - (int64_t)k * chunk < chunk ? length - (int64_t)k * chunk : chunk);
+        named_barrier_sync(1 + b, kTileBlock);
         if (lane < T) {
-          for (int i = lane; i < count; i += T, bit += width) {
-            const uint64_t w = bit >> 5;
-            column += (int)(__funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1), (uint32_t)(bit & 31)) & mask);
-            s_columns[i] = column;
-          }
-        }
-        __syncthreads();
-      }
+          const V* v = s_values + b * chunk;
+          const V* g = s_x + b * chunk;
 #pragma unroll 8
-      for (int i = threadIdx.x; i < count; i += kTileBlock) {
-        const int64_t e = begin + first + i;
-        const int c = kPacked ? s_columns[i] : base + (int)load_readonly(index + e);
-        s_values[i] = load_readonly(values + e);
-        s_x[i] = load_readonly(x + c);
+          for (int i = lane; i < count; i += T) sum = VT::fma(VT::widen(v[i]), VT::widen(g[i]), sum);
+        }
+        named_barrier_arrive(3 + b, kTileBlock);
       }
-      __syncthreads();
-      if (lane < T)
-        for (int i = lane; i < count; i += T) sum = VT::fma(VT::widen(s_values[i]), VT::widen(s_x[i]), sum);
-      __syncthreads();
-    }
-    if (threadIdx.x < 32) {
 #pragma unroll
       for (int offset = T / 2; offset > 0; offset >>= 1) sum = VT::add(sum, __shfl_down_sync(0xffffffffu, sum, offset, T));
-      if (threadIdx.x == 0) y[row] = VT::narrow(sum);
+      if (lane == 0) static_cast<V*>(a.y)[row] = VT::narrow(sum);
+    } else {
+      const int base = kBase ? a.row_base[row] : 0;
+      // CSR-lp lane state (lane owners among the producers): the next delta's bit and the running column
+      const int quotient = (int)(length / T), remainder = (int)(length - (int64_t)quotient * T);
+      const uint32_t width = kPacked ? a.row_width[row] : 0u;
+      const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
+      const uint32_t* words = kPacked ? a.words + a.row_word[row] : nullptr;
+      uint64_t bit = kPacked && producer < T
+                         ? (uint64_t)width * (uint64_t)(producer * quotient + (producer < remainder ? producer : remainder))
+                         : 0;
+      int column = base;
+      for (int k = 0; k < chunks; ++k) {
+        const int b = k & 1;
+        const int count = (int)(length - (int64_t)k * chunk < chunk ? length - (int64_t)k * chunk : chunk);
+        if (k >= 2) named_barrier_sync(3 + b, kTileBlock);   // the consumer is done with chunk k - 2
+        int* columns = s_columns + b * chunk;
+        if constexpr (kPacked) {
+          if (producer < T) {
+            for (int i = producer; i < count; i += T, bit += width) {
+              const uint64_t w = bit >> 5;
+              column += (int)(__funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1), (uint32_t)(bit & 31)) & mask);
+              columns[i] = column;
+            }
+          }
+          named_barrier_sync(5, kLongProducers);
+        }
+        const int64_t first = begin + (int64_t)k * chunk;
+        V* v = s_values + b * chunk;
+        V* g = s_x + b * chunk;
+#pragma unroll 8
+        for (int i = producer; i < count; i += kLongProducers) {
+          const int c = kPacked ? columns[i] : base + (int)load_readonly(index + first + i);
+          v[i] = load_readonly(values + first + i);
+          g[i] = load_readonly(x + c);
+        }
+        named_barrier_arrive(1 + b, kTileBlock);
+      }
+      // the next row refills the buffers: wait until the consumer has released the last ones
+      for (int k = chunks >= 2 ? chunks - 2 : 0; k < chunks; ++k) named_barrier_sync(3 + (k & 1), kTileBlock);
     }
   }
+}
+
+// ---- rows by length (k_spmv_classes) ------------------------------------------------------------------
+// For matrices whose nonzeros sit in rows of very different lengths, rows are classed by length and each
+// class runs on its own mapping straight from global memory (no tiles): short rows (at most kShortMax
+// entries) one per thread, several per thread at once; longer rows from a list, each on P threads with P
+// chosen per row (the fewest, with at most 8 lane sums a thread, that leave a thread at most 32 of its
+// entries; segments of equal P, longest rows first); rows longer than the long-row threshold one per CTA (long_rows above). The summation order
+// is the same in every class.
+constexpr int kShortMax = 8;
+// x values a thread of a listed row gathers at once (the class kernel runs 4 CTAs of 256 threads per
+// multiprocessor, 64 registers a thread)
+template <class V> struct ClassGathers { static constexpr int value = sizeof(V) == 8 ? 8 : 16; };
+
+template <class V> struct ShortRowsPerThread { static constexpr int value = sizeof(V) == 8 ? 1 : 2; };
+
+// Rows chunk * 256U + u * 256 + threadIdx.x (u < U) of the matrix; rows longer than kShortMax are left to
+// the listed and long rows. Entry j of a short row is entry j / W of logical lane j % W, W = min(T, kShortMax).
+// For T > W the lanes W..T-1 are empty (+0): the tree levels with offsets >= W add +0 to each of the first
+// W lane sums (which only turns a -0 into +0, once), and the levels below W are the tree of W lanes.
+template <class V, int LAYOUT, int T>
+__device__ __forceinline__ void short_rows(const KernelArgs& a, int64_t chunk) {
+  using VT = ValueTraits<V>;
+  using Acc = typename VT::Acc;
+  constexpr int U = ShortRowsPerThread<V>::value;
+  constexpr int W = T < kShortMax ? T : kShortMax;
+  constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
+  constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
+  const GlobalView<V, LAYOUT> g(a);
+  const V* x = static_cast<const V*>(a.x);
+  V* y = static_cast<V*>(a.y);
+  int row[U], begin[U], length[U];
+  bool mine[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int64_t r = chunk * (int64_t)(kTileBlock * U) + u * kTileBlock + threadIdx.x;
+    row[u] = (int)r;
+    mine[u] = r < a.rows;
+    begin[u] = mine[u] ? g.row_ptr(row[u]) : 0;
+    length[u] = mine[u] ? g.row_ptr(row[u] + 1) - begin[u] : 0;
+    mine[u] = mine[u] && length[u] <= kShortMax;
+  }
+  V xv[U][kShortMax];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if constexpr (!kPacked) {
+      const int base = kBase && mine[u] ? g.row_base(row[u]) : 0;
+#pragma unroll
+      for (int j = 0; j < kShortMax; ++j)
+        if (mine[u] && j < length[u]) xv[u][j] = load_readonly(x + base + (int)g.index(begin[u] + j));
+    } else {
+      if (mine[u] && length[u] > 0) {
+        const int quotient = length[u] / T, remainder = length[u] - quotient * T;
+        const uint32_t width = g.row_width(row[u]);
+        const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
+        const int64_t w0 = g.row_word(row[u]);
+        int column[W];
+        const int base = g.row_base(row[u]);
+#pragma unroll
+        for (int l = 0; l < W; ++l) column[l] = base;
+#pragma unroll
+        for (int j = 0; j < kShortMax; ++j) {
+          const int lane = j % W, k = j / W;
+          if (j < length[u]) {
+            const uint32_t delta = (uint32_t)(lane * quotient + (lane < remainder ? lane : remainder) + k);
+            column[lane] += (int)packed_delta(g, w0, delta * width, mask);
+            xv[u][j] = load_readonly(x + column[lane]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    Acc acc[W];
+#pragma unroll
+    for (int l = 0; l < W; ++l) acc[l] = Acc(0);
+#pragma unroll
+    for (int j = 0; j < kShortMax; ++j)
+      if (mine[u] && j < length[u]) acc[j % W] = VT::fma(VT::widen(g.value(begin[u] + j)), VT::widen(xv[u][j]), acc[j % W]);
+    if constexpr (T > W) {
+#pragma unroll
+      for (int l = 0; l < W; ++l) acc[l] = VT::add(acc[l], Acc(0));
+    }
+#pragma unroll
+    for (int offset = W / 2; offset > 0; offset >>= 1)
+#pragma unroll
+      for (int l = 0; l < offset; ++l) acc[l] = VT::add(acc[l], acc[l + offset]);
+    if (mine[u]) y[row[u]] = VT::narrow(acc[0]);
+  }
+}
+
+// Items chunk * (256 / P) + group of segment `segment` of the row items, one row per group of P threads.
+template <class V, int LAYOUT, int T, int P>
+__device__ __forceinline__ void listed_rows(const KernelArgs& a, int segment, int64_t chunk) {
+  using VT = ValueTraits<V>;
+  const int group = threadIdx.x / P, p = threadIdx.x % P;
+  const int64_t index = chunk * (kTileBlock / P) + group;
+  const bool active = index < a.segment_items[segment];
+  const int4 item = active ? __ldg(a.row_items + a.segment_first[segment] + index) : make_int4(0, 0, 0, 0);
+  const GlobalView<V, LAYOUT> g(a);
+  const auto sum = row_product<V, LAYOUT, T, P, ClassGathers<V>::value>(g, static_cast<const V*>(a.x), item.x, item.y, item.z,
+                                                                item.w, active, p);
+  if (p == 0 && active) static_cast<V*>(a.y)[item.x] = VT::narrow(sum);
+}
+
+// The segments that exist for T: P divides T with T / P <= 8 (at most 8 lane sums a thread).
+__host__ __device__ constexpr bool segment_exists(int tpr, int segment) {
+  return (1 << segment) <= tpr && tpr / (1 << segment) <= 8;
+}
+
+template <class V, int LAYOUT, int T, int SEGMENT>
+__device__ __forceinline__ bool run_segment(const KernelArgs& a, int64_t& block) {
+  if constexpr (segment_exists(T, SEGMENT)) {
+    if (block < a.segment_blocks[SEGMENT]) {
+      listed_rows<V, LAYOUT, T, (1 << SEGMENT)>(a, SEGMENT, block);
+      return true;
+    }
+    block -= a.segment_blocks[SEGMENT];
+  }
+  return false;
+}
+
+// Blocks [0, long_blocks): one long row each; then the segments from P = 32 down to P = 1; then short rows.
+template <class V, int LAYOUT, int T>
+__global__ void __launch_bounds__(kTileBlock, 4) k_spmv_classes(const KernelArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  int64_t block = blockIdx.x;
+  if (block < a.long_blocks) {
+    long_rows<V, LAYOUT, T>(a, smem, block, a.long_blocks);
+    return;
+  }
+  block -= a.long_blocks;
+  if (run_segment<V, LAYOUT, T, 5>(a, block) || run_segment<V, LAYOUT, T, 4>(a, block) ||
+      run_segment<V, LAYOUT, T, 3>(a, block) || run_segment<V, LAYOUT, T, 2>(a, block) ||
+      run_segment<V, LAYOUT, T, 1>(a, block) || run_segment<V, LAYOUT, T, 0>(a, block))
+    return;
+  short_rows<V, LAYOUT, T>(a, block);
 }
 
 // ---- k_spmv_tiles --------------------------------------------------------------------------------------

@@ -87,7 +87,50 @@ cudaError_t vector_for_layout(int tpr, const KernelArgs& a, int64_t blocks, cuda
   }
 }
 
+// mode 0: launch k_spmv_classes over `blocks` CTAs; mode 1: raise its shared-memory limit to smem
+template <class V, int L, int T>
+cudaError_t classes_variant(int mode, const KernelArgs& a, int64_t blocks, int smem, cudaStream_t stream) {
+  if (mode == 1) return cudaFuncSetAttribute(k_spmv_classes<V, L, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (blocks <= 0) return cudaSuccess;
+  k_spmv_classes<V, L, T><<<(unsigned)blocks, kTileBlock, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <class V, int L>
+cudaError_t classes_for_layout(int tpr, int mode, const KernelArgs& a, int64_t blocks, int smem, cudaStream_t stream) {
+  switch (tpr) {
+    case 2: return classes_variant<V, L, 2>(mode, a, blocks, smem, stream);
+    case 4: return classes_variant<V, L, 4>(mode, a, blocks, smem, stream);
+    case 8: return classes_variant<V, L, 8>(mode, a, blocks, smem, stream);
+    case 16: return classes_variant<V, L, 16>(mode, a, blocks, smem, stream);
+    case 32: return classes_variant<V, L, 32>(mode, a, blocks, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <class V>
+cudaError_t classes_for_value(int layout, int tpr, int mode, const KernelArgs& a, int64_t blocks, int smem, cudaStream_t stream) {
+  switch (layout) {
+    case SPMV_LAYOUT_I32: return classes_for_layout<V, SPMV_LAYOUT_I32>(tpr, mode, a, blocks, smem, stream);
+    case SPMV_LAYOUT_I16: return classes_for_layout<V, SPMV_LAYOUT_I16>(tpr, mode, a, blocks, smem, stream);
+    case SPMV_LAYOUT_R16: return classes_for_layout<V, SPMV_LAYOUT_R16>(tpr, mode, a, blocks, smem, stream);
+    case SPMV_LAYOUT_LP:  return classes_for_layout<V, SPMV_LAYOUT_LP>(tpr, mode, a, blocks, smem, stream);
+    case SPMV_LAYOUT_I8:  return classes_for_layout<V, SPMV_LAYOUT_I8>(tpr, mode, a, blocks, smem, stream);
+    case SPMV_LAYOUT_R8:  return classes_for_layout<V, SPMV_LAYOUT_R8>(tpr, mode, a, blocks, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 }  // namespace
+
+cudaError_t LAUNCH_CLASSES_NAME(int layout, int tpr, const KernelArgs& a, int64_t blocks, int smem, cudaStream_t stream) {
+  return classes_for_value<VALUE_TYPE>(layout, tpr, 0, a, blocks, smem, stream);
+}
+
+cudaError_t PREPARE_CLASSES_NAME(int layout, int tpr, int smem) {
+  const KernelArgs unused{};
+  return classes_for_value<VALUE_TYPE>(layout, tpr, 1, unused, 0, smem, nullptr);
+}
 
 cudaError_t LAUNCH_TILES_NAME(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream) {
   return tiles_for_value<VALUE_TYPE>(layout, tpr, physical_tpr, 0, a, stream, 0, nullptr);

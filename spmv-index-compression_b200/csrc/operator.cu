@@ -119,6 +119,55 @@ int choose_physical_tpr(int tpr, int layout, double mean_length) {
   return physical;
 }
 
+// Rows by length: the nonzeros of rows longer than 4x the mean + 32 make at least a tenth of the matrix
+// (a power-law graph), so that tiles of consecutive rows would mix very short and very long rows.
+bool skewed_rows(const Csr& matrix) {
+  if (matrix.rows == 0 || matrix.nnz() == 0) return false;
+  const double heavy = 4.0 * (double)matrix.nnz() / matrix.rows + 32.0;
+  int64_t heavy_nnz = 0;
+  for (int row = 0; row < matrix.rows; ++row) {
+    const int length = matrix.row_ptr[row + 1] - matrix.row_ptr[row];
+    if (length > heavy) heavy_nnz += length;
+  }
+  return heavy_nnz * 10 >= matrix.nnz();
+}
+
+// Rows by length: rows of at most kShortMax entries need no list (their blocks walk all rows); rows up to
+// long_threshold are listed as {row, first entry, end entry, row base} items, each in the segment of its
+// P (the fewest threads, among the P that divide T with T / P <= 8, that leave a thread at most 32 of
+// its entries), longest first within a segment; longer rows are long rows, one CTA each.
+struct ClassPlan {
+  std::vector<int4> items;
+  int64_t segment_first[6] = {0, 0, 0, 0, 0, 0};
+  int64_t segment_items[6] = {0, 0, 0, 0, 0, 0};
+  std::vector<int> long_rows;
+};
+
+ClassPlan plan_classes(const Csr& matrix, int tpr, int long_threshold) {
+  ClassPlan plan;
+  std::vector<int4> segments[6];
+  for (int row = 0; row < matrix.rows; ++row) {
+    const int begin = matrix.row_ptr[row], length = matrix.row_ptr[row + 1] - begin;
+    if (length <= kShortMax) continue;
+    if (length > long_threshold) {
+      plan.long_rows.push_back(row);
+      continue;
+    }
+    int segment = 0;
+    while (!segment_exists(tpr, segment)) ++segment;
+    while (segment < 5 && segment_exists(tpr, segment + 1) && length > 32 * (1 << segment)) ++segment;
+    segments[segment].push_back(make_int4(row, begin, begin + length, matrix.col_ind[begin]));
+  }
+  for (int segment = 0; segment < 6; ++segment) {
+    std::stable_sort(segments[segment].begin(), segments[segment].end(),
+                     [](const int4& a, const int4& b) { return a.z - a.y > b.z - b.y; });
+    plan.segment_first[segment] = (int64_t)plan.items.size();
+    plan.segment_items[segment] = (int64_t)segments[segment].size();
+    plan.items.insert(plan.items.end(), segments[segment].begin(), segments[segment].end());
+  }
+  return plan;
+}
+
 }  // namespace spmvb200
 
 struct spmv_operator {
@@ -145,13 +194,21 @@ struct spmv_operator {
   int long_chunk = 0;
   int smem_bytes = 0;
   int64_t device_bytes = 0;
+  // rows by length (SPMV_SCHEDULE_CLASSES)
+  int schedule = SPMV_SCHEDULE_TILES;
+  int4* row_items = nullptr;
+  int64_t segment_first[6] = {0, 0, 0, 0, 0, 0};
+  int64_t segment_items[6] = {0, 0, 0, 0, 0, 0};
+  int64_t segment_blocks[6] = {0, 0, 0, 0, 0, 0};
+  int64_t short_blocks = 0;
 
   ~spmv_operator() {
     int previous = -1;
     cudaGetDevice(&previous);
     if (previous != device) cudaSetDevice(device);
     for (void* pointer : {(void*)row_ptr, values, columns, (void*)row_base, (void*)row_word, (void*)row_width,
-                          (void*)words, (void*)tiles, (void*)tile_words, (void*)long_rows, (void*)status})
+                          (void*)words, (void*)tiles, (void*)tile_words, (void*)long_rows, (void*)status,
+                          (void*)row_items})
       if (pointer) cudaFree(pointer);
     if (previous >= 0 && previous != device) cudaSetDevice(previous);
   }
@@ -187,7 +244,26 @@ KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   a.long_chunk = op->long_chunk;
   a.smem_bytes = op->smem_bytes;
   a.status = op->status;
+  a.row_items = op->row_items;
+  a.long_blocks = op->schedule == SPMV_SCHEDULE_CLASSES ? op->long_count : 0;
+  for (int segment = 0; segment < 6; ++segment) {
+    a.segment_first[segment] = op->segment_first[segment];
+    a.segment_items[segment] = op->segment_items[segment];
+    a.segment_blocks[segment] = op->segment_blocks[segment];
+  }
   return a;
+}
+
+int64_t class_blocks(const spmv_operator* op) {
+  int64_t blocks = op->long_count + op->short_blocks;
+  for (int segment = 0; segment < 6; ++segment) blocks += op->segment_blocks[segment];
+  return blocks;
+}
+
+cudaError_t launch_product(const spmv_operator* op, const KernelArgs& a, cudaStream_t stream) {
+  if (op->schedule == SPMV_SCHEDULE_CLASSES)
+    return launch_classes(op->dtype, op->layout, op->tpr, a, class_blocks(op), op->smem_bytes, stream);
+  return launch_tiles(op->dtype, op->layout, op->tpr, op->physical_tpr, a, stream);
 }
 
 }  // namespace
@@ -258,8 +334,12 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
       while (op->tile_nnz > 256 && tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages) > budget)
         op->tile_nnz -= 256;
     }
+    require(config->schedule >= SPMV_SCHEDULE_AUTO && config->schedule <= SPMV_SCHEDULE_CLASSES,
+            "schedule must be SPMV_SCHEDULE_AUTO, _TILES or _CLASSES");
+    op->schedule = config->schedule != SPMV_SCHEDULE_AUTO ? config->schedule
+                                                          : (skewed_rows(m) ? SPMV_SCHEDULE_CLASSES : SPMV_SCHEDULE_TILES);
     const int smem = tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages);
-    if (smem > shared_limit)
+    if (op->schedule == SPMV_SCHEDULE_TILES && smem > shared_limit)
       fail(SPMV_ERR_INVALID_ARGUMENT, "tiles need " + std::to_string(smem) + " bytes of shared memory, above the " +
                                           std::to_string(shared_limit) + " a block may have");
 
@@ -307,6 +387,37 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
       op->row_base = device_upload<int>(bases.data(), bases.size(), op->device_bytes);
     }
 
+    op->status = device_upload<unsigned>(nullptr, 1, op->device_bytes);
+    cuda_check(cudaMemset(op->status, 0, sizeof(unsigned)), "cudaMemset");
+    if (op->schedule == SPMV_SCHEDULE_CLASSES) {
+      // rows by length; long rows (above 64 T entries) one CTA each, in double-buffered chunks of 2048
+      // entries (1024 for FP64) held in shared memory
+      const ClassPlan plan = plan_classes(m, tpr, 64 * tpr);
+      op->long_count = (int64_t)plan.long_rows.size();
+      op->row_items = device_upload<int4>(plan.items.data(), plan.items.size(), op->device_bytes);
+      op->long_rows = device_upload<int>(plan.long_rows.data(), plan.long_rows.size(), op->device_bytes);
+      op->long_chunk = value_bytes == 8 ? 1024 : 2048;
+      op->smem_bytes = op->long_count > 0 ? long_smem_bytes(op->long_chunk, value_bytes, layout == SPMV_LAYOUT_LP) : 0;
+      int64_t blocks = op->long_count;
+      for (int segment = 0; segment < 6; ++segment) {
+        const int per_block = kTileBlock >> segment;
+        op->segment_first[segment] = plan.segment_first[segment];
+        op->segment_items[segment] = plan.segment_items[segment];
+        op->segment_blocks[segment] = (plan.segment_items[segment] + per_block - 1) / per_block;
+        blocks += op->segment_blocks[segment];
+      }
+      const int short_rows_per_block = kTileBlock * (dtype == SPMV_F64 ? ShortRowsPerThread<double>::value
+                                                                       : ShortRowsPerThread<float>::value);
+      op->short_blocks = ((int64_t)m.rows + short_rows_per_block - 1) / short_rows_per_block;
+      blocks += op->short_blocks;
+      if (blocks > 0x7fffffff)
+        fail(SPMV_ERR_TOO_LARGE, "grid exceeds 2^31-1 blocks");
+      cuda_check(prepare_classes(dtype, layout, tpr, op->smem_bytes), "class kernel shared memory");
+      cuda_check(cudaDeviceSynchronize(), "operator upload");
+      *out = op.release();
+      return;
+    }
+
     // tile plan
     const TilePlan plan = plan_tiles(m, op->tile_nnz, op->tile_rows, layout == SPMV_LAYOUT_LP ? row_word.data() : nullptr,
                                      layout == SPMV_LAYOUT_LP ? row_width.data() : nullptr);
@@ -316,13 +427,12 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     if (layout == SPMV_LAYOUT_LP)
       op->tile_words = device_upload<int2>(plan.tile_words.data(), plan.tile_words.size(), op->device_bytes);
     op->long_rows = device_upload<int>(plan.long_rows.data(), plan.long_rows.size(), op->device_bytes);
-    op->status = device_upload<unsigned>(nullptr, 1, op->device_bytes);
-    cuda_check(cudaMemset(op->status, 0, sizeof(unsigned)), "cudaMemset");
     // long rows: one CTA per row at a time; a chunk of a long row (values, gathered x and, for CSR-lp,
     // decoded columns) lives in the CTA's shared memory, at least kTileBlock entries, at most 8192, and
     // the launch gets the larger of the tile buffers and one chunk
-    op->long_chunk = std::max(kTileBlock, std::min(8192, (smem / (2 * value_bytes + 4)) / kTileBlock * kTileBlock));
-    op->smem_bytes = std::max(smem, op->long_count > 0 ? op->long_chunk * (2 * value_bytes + 4) : 0);
+    const bool packed = layout == SPMV_LAYOUT_LP;
+    op->long_chunk = std::max(kTileBlock, std::min(8192, (smem / long_smem_bytes(1, value_bytes, packed)) / kTileBlock * kTileBlock));
+    op->smem_bytes = std::max(smem, op->long_count > 0 ? long_smem_bytes(op->long_chunk, value_bytes, packed) : 0);
     if (op->smem_bytes > shared_limit) fail(SPMV_ERR_INVALID_ARGUMENT, "long-row chunk exceeds the shared memory of a block");
     // persistent tile CTAs: as many as fit on the device at once, never more than there are tiles
     const int resident = tiles_occupancy(dtype, layout, tpr, op->physical_tpr, op->smem_bytes);
@@ -354,6 +464,10 @@ int spmv_operator_get_info(const spmv_operator* op, spmv_operator_info* info) {
     info->long_rows = op->long_count;
     info->device_bytes = op->device_bytes;
     info->memory = op->memory;
+    info->schedule = op->schedule;
+    info->listed_rows = 0;
+    for (int segment = 0; segment < 6; ++segment) info->listed_rows += op->segment_items[segment];
+    info->blocks = op->schedule == SPMV_SCHEDULE_CLASSES ? class_blocks(op) : op->long_ctas + op->tile_ctas;
   });
 }
 
@@ -369,9 +483,7 @@ int spmv_operator_run(const spmv_operator* op, const void* x, void* y, void* str
   return guarded([&] {
     require(op && x && y, "op, x and y are required");
     check_vector_alignment(op, x, y);
-    const KernelArgs a = kernel_args(op, x, y);
-    cuda_check(launch_tiles(op->dtype, op->layout, op->tpr, op->physical_tpr, a, static_cast<cudaStream_t>(stream)),
-               "SpMV launch");
+    cuda_check(launch_product(op, kernel_args(op, x, y), static_cast<cudaStream_t>(stream)), "SpMV launch");
   });
 }
 
@@ -383,8 +495,7 @@ int spmv_operator_run_host(const spmv_operator* op, const void* x_host, void* y_
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t value_bytes = (size_t)value_bytes_of(op->dtype);
     cuda_check(cudaMemcpyAsync(x_device, x_host, value_bytes * op->cols, cudaMemcpyHostToDevice, s), "copy x");
-    const KernelArgs a = kernel_args(op, x_device, y_device);
-    cuda_check(launch_tiles(op->dtype, op->layout, op->tpr, op->physical_tpr, a, s), "SpMV launch");
+    cuda_check(launch_product(op, kernel_args(op, x_device, y_device), s), "SpMV launch");
     cuda_check(cudaMemcpyAsync(y_host, y_device, value_bytes * op->rows, cudaMemcpyDeviceToHost, s), "copy y");
     cuda_check(cudaStreamSynchronize(s), "stream synchronize");
   });

@@ -39,6 +39,7 @@ DTYPE_BY_NAME = {name: code for code, name in DTYPE_NAMES.items()}
 NUMPY_DTYPES = {F64: np.float64, F32: np.float32, F16: np.float16}
 VALUE_BYTES = {F64: 8, F32: 4, F16: 2}
 THREADS_PER_ROW = (2, 4, 8, 16, 32)
+SCHEDULE_AUTO, SCHEDULE_TILES, SCHEDULE_CLASSES = 0, 1, 2
 
 OK = 0
 ERR_INVALID_ARGUMENT, ERR_IO, ERR_FORMAT, ERR_NOT_ADMISSIBLE, ERR_OUT_OF_MEMORY = 1, 2, 3, 4, 5
@@ -89,7 +90,8 @@ class MemoryBreakdown(ctypes.Structure):
 class OperatorConfig(ctypes.Structure):
     _fields_ = [("layout", ctypes.c_int), ("dtype", ctypes.c_int), ("tpr", ctypes.c_int),
                 ("physical_tpr", ctypes.c_int), ("tile_nnz", ctypes.c_int), ("value_rounding", ctypes.c_int),
-                ("device", ctypes.c_int), ("stages", ctypes.c_int), ("tile_rows", ctypes.c_int)]
+                ("device", ctypes.c_int), ("stages", ctypes.c_int), ("tile_rows", ctypes.c_int),
+                ("schedule", ctypes.c_int)]
 
 
 class OperatorInfo(ctypes.Structure):
@@ -97,7 +99,8 @@ class OperatorInfo(ctypes.Structure):
                 ("dtype", ctypes.c_int), ("tpr", ctypes.c_int), ("physical_tpr", ctypes.c_int),
                 ("tile_nnz", ctypes.c_int), ("tiles", ctypes.c_int64), ("tile_ctas", ctypes.c_int64),
                 ("stages", ctypes.c_int), ("tile_rows", ctypes.c_int), ("long_rows", ctypes.c_int64),
-                ("device_bytes", ctypes.c_int64), ("memory", MemoryBreakdown)]
+                ("device_bytes", ctypes.c_int64), ("memory", MemoryBreakdown), ("schedule", ctypes.c_int),
+                ("listed_rows", ctypes.c_int64), ("blocks", ctypes.c_int64)]
 
 
 class OperatorArrays(ctypes.Structure):
@@ -496,7 +499,8 @@ class Operator:
     """A matrix encoded in one layout and uploaded to a GPU; run() is launch<T> at the operator's T."""
 
     def __init__(self, matrix: CsrMatrix, layout: int, dtype: int, tpr: int, physical_tpr: int = 0,
-                 tile_nnz: int = 0, value_rounding: int = 0, device: int = -1, stages: int = 0, tile_rows: int = 0):
+                 tile_nnz: int = 0, value_rounding: int = 0, device: int = -1, stages: int = 0, tile_rows: int = 0,
+                 schedule: int = 0):
         config = OperatorConfig()
         _lib.spmv_operator_config_init(ctypes.byref(config), layout, dtype, tpr)
         config.physical_tpr = physical_tpr
@@ -505,6 +509,7 @@ class Operator:
         config.device = device
         config.stages = stages
         config.tile_rows = tile_rows
+        config.schedule = schedule
         handle = ctypes.c_void_p()
         _check(_lib.spmv_operator_create(matrix.handle, ctypes.byref(config), ctypes.byref(handle)))
         self._handle = handle
