@@ -95,6 +95,7 @@ struct KernelArgs {
   int64_t tile_count;
   int tile_nnz;              // nonzeros a tile holds at most
   int tile_rows;             // rows a tile holds at most
+  int tile_index_words;      // CSR-lp: stream words a tile's image holds at most
   int stages;                // shared-memory buffers of a tile CTA (1..kMaxStages)
   const int* row_list;       // rows of the vector path (nullptr: rows 0..row_count-1)
   int64_t row_count;         // entries of row_list, or rows
@@ -123,7 +124,9 @@ struct StagePlan {
 
 __host__ __device__ inline int round16(int bytes) { return (bytes + 15) & ~15; }
 
-__host__ __device__ inline StagePlan stage_plan(int tile_nnz, int tile_rows, int value_bytes, int layout) {
+// index_words: CSR-lp, the words a tile's stream image holds at most (the longest tile's word range plus
+// the word a delta may read past it); ignored by the other layouts, whose index image holds tile_nnz.
+__host__ __device__ inline StagePlan stage_plan(int tile_nnz, int tile_rows, int value_bytes, int layout, int index_words) {
   const bool base = layout == SPMV_LAYOUT_R16 || layout == SPMV_LAYOUT_R8 || layout == SPMV_LAYOUT_LP;
   const bool packed = layout == SPMV_LAYOUT_LP;
   const int index_bytes = packed ? 4 : (layout == SPMV_LAYOUT_I32 ? 4 : ((layout == SPMV_LAYOUT_I16 || layout == SPMV_LAYOUT_R16) ? 2 : 1));
@@ -135,13 +138,14 @@ __host__ __device__ inline StagePlan stage_plan(int tile_nnz, int tile_rows, int
   plan.row_word = offset;  if (packed) offset += round16(4 * tile_rows) + 16;
   plan.row_width = offset; if (packed) offset += round16(tile_rows) + 16;
   plan.values = offset;    offset += round16(value_bytes * tile_nnz) + 16;
-  plan.index = offset;     offset += packed ? round16(4 * (tile_nnz + 1)) + 16 : round16(index_bytes * tile_nnz) + 16;
+  plan.index = offset;     offset += packed ? round16(4 * index_words) + 16 : round16(index_bytes * tile_nnz) + 16;
   plan.bytes = offset;
   return plan;
 }
 
-__host__ __device__ inline int tile_smem_bytes(int tile_nnz, int tile_rows, int value_bytes, int layout, int stages) {
-  return 64 + stages * stage_plan(tile_nnz, tile_rows, value_bytes, layout).bytes;
+__host__ __device__ inline int tile_smem_bytes(int tile_nnz, int tile_rows, int value_bytes, int layout, int stages,
+                                               int index_words) {
+  return 64 + stages * stage_plan(tile_nnz, tile_rows, value_bytes, layout, index_words).bytes;
 }
 
 // ---- small device helpers -----------------------------------------------------------------------
@@ -571,11 +575,27 @@ __host__ __device__ inline int long_smem_bytes(int chunk, int value_bytes, bool 
   return 4 * chunk * value_bytes + (packed ? 8 * chunk : 0);
 }
 
-__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
-  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+// Named barriers with immediate ids, so that the kernel reserves only the barriers it uses.
+template <int ID, int THREADS>
+__device__ __forceinline__ void named_barrier_sync() {
+  asm volatile("barrier.sync %0, %1;" ::"n"(ID), "n"(THREADS) : "memory");
 }
-__device__ __forceinline__ void named_barrier_arrive(int id, int threads) {
-  asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+template <int ID, int THREADS>
+__device__ __forceinline__ void named_barrier_arrive() {
+  asm volatile("barrier.arrive %0, %1;" ::"n"(ID), "n"(THREADS) : "memory");
+}
+// buffer b of a long-row CTA: full (producers arrive, the consumer waits) and free (the reverse)
+__device__ __forceinline__ void long_full_sync(int b) {
+  if (b == 0) named_barrier_sync<1, kTileBlock>(); else named_barrier_sync<2, kTileBlock>();
+}
+__device__ __forceinline__ void long_full_arrive(int b) {
+  if (b == 0) named_barrier_arrive<1, kTileBlock>(); else named_barrier_arrive<2, kTileBlock>();
+}
+__device__ __forceinline__ void long_free_sync(int b) {
+  if (b == 0) named_barrier_sync<3, kTileBlock>(); else named_barrier_sync<4, kTileBlock>();
+}
+__device__ __forceinline__ void long_free_arrive(int b) {
+  if (b == 0) named_barrier_arrive<3, kTileBlock>(); else named_barrier_arrive<4, kTileBlock>();
 }
 
 template <class V, int LAYOUT, int T>
@@ -609,14 +629,14 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
       for (int k = 0; k < chunks; ++k) {
         const int b = k & 1;
         const int count = (int)(length - (int64_t)k * chunk < chunk ? length - (int64_t)k * chunk : chunk);
-        named_barrier_sync(1 + b, kTileBlock);
+        long_full_sync(b);
         if (lane < T) {
           const V* v = s_values + b * chunk;
           const V* g = s_x + b * chunk;
 #pragma unroll 8
           for (int i = lane; i < count; i += T) sum = VT::fma(VT::widen(v[i]), VT::widen(g[i]), sum);
         }
-        named_barrier_arrive(3 + b, kTileBlock);
+        long_free_arrive(b);
       }
 #pragma unroll
       for (int offset = T / 2; offset > 0; offset >>= 1) sum = VT::add(sum, __shfl_down_sync(0xffffffffu, sum, offset, T));
@@ -635,7 +655,7 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
       for (int k = 0; k < chunks; ++k) {
         const int b = k & 1;
         const int count = (int)(length - (int64_t)k * chunk < chunk ? length - (int64_t)k * chunk : chunk);
-        if (k >= 2) named_barrier_sync(3 + b, kTileBlock);   // the consumer is done with chunk k - 2
+        if (k >= 2) long_free_sync(b);   // the consumer is done with chunk k - 2
         int* columns = s_columns + b * chunk;
         if constexpr (kPacked) {
           if (producer < T) {
@@ -645,7 +665,7 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
               columns[i] = column;
             }
           }
-          named_barrier_sync(5, kLongProducers);
+          named_barrier_sync<5, kLongProducers>();
         }
         const int64_t first = begin + (int64_t)k * chunk;
         V* v = s_values + b * chunk;
@@ -656,10 +676,10 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
           v[i] = load_readonly(values + first + i);
           g[i] = load_readonly(x + c);
         }
-        named_barrier_arrive(1 + b, kTileBlock);
+        long_full_arrive(b);
       }
       // the next row refills the buffers: wait until the consumer has released the last ones
-      for (int k = chunks >= 2 ? chunks - 2 : 0; k < chunks; ++k) named_barrier_sync(3 + (k & 1), kTileBlock);
+      for (int k = chunks >= 2 ? chunks - 2 : 0; k < chunks; ++k) long_free_sync(k & 1);
     }
   }
 }
@@ -818,7 +838,7 @@ __global__ void __launch_bounds__(kTileBlock, 2) k_spmv_tiles(const KernelArgs a
   __shared__ int s_abort;
   __shared__ int s_released[kMaxStages];   // warps done with the buffer's current tile
   __shared__ int s_fills[kMaxStages];      // bulk fills issued into the buffer so far
-  const StagePlan plan = stage_plan(a.tile_nnz, a.tile_rows, (int)sizeof(V), LAYOUT);
+  const StagePlan plan = stage_plan(a.tile_nnz, a.tile_rows, (int)sizeof(V), LAYOUT, a.tile_index_words);
   const int stages = a.stages;
   const int64_t cta = (int64_t)blockIdx.x - a.vector_blocks;
   const int64_t ctas = (int64_t)gridDim.x - a.vector_blocks;

@@ -70,6 +70,7 @@ struct TilePlan {
   std::vector<int> long_rows;
   int64_t short_rows = 0;
   int64_t short_nnz = 0;
+  int index_words = 0;   // CSR-lp: the longest tile's word range plus one
 };
 
 TilePlan plan_tiles(const Csr& matrix, int tile_nnz, int tile_rows, const int* row_word, const uint8_t* row_width) {
@@ -83,6 +84,7 @@ TilePlan plan_tiles(const Csr& matrix, int tile_nnz, int tile_rows, const int* r
       const int last = end - 1;
       const int64_t last_words = ((int64_t)(matrix.row_ptr[last + 1] - matrix.row_ptr[last]) * row_width[last] + 31) / 32;
       plan.tile_words.push_back(make_int2(row_word[begin], (int)(row_word[last] + last_words)));
+      plan.index_words = std::max(plan.index_words, (int)(row_word[last] + last_words) + 1 - row_word[begin]);
     }
     begin = -1;
     count = 0;
@@ -172,7 +174,7 @@ ClassPlan plan_classes(const Csr& matrix, int tpr, int long_threshold) {
 
 struct spmv_operator {
   int device = 0;
-  int layout = 0, dtype = 0, tpr = 0, physical_tpr = 0, tile_nnz = 0, tile_rows = 0, stages = 0;
+  int layout = 0, dtype = 0, tpr = 0, physical_tpr = 0, tile_nnz = 0, tile_rows = 0, stages = 0, tile_index_words = 0;
   int rows = 0, cols = 0;
   int64_t nnz = 0;
   spmv_memory memory{};
@@ -236,6 +238,7 @@ KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   a.tile_count = op->tile_count;
   a.tile_nnz = op->tile_nnz;
   a.tile_rows = op->tile_rows;
+  a.tile_index_words = op->tile_index_words;
   a.stages = op->stages;
   a.tile_ctas = op->tile_ctas;
   a.row_list = op->long_rows;
@@ -319,29 +322,17 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     op->physical_tpr = config->physical_tpr > 0 ? config->physical_tpr : choose_physical_tpr(tpr, layout, mean_length);
     op->tile_rows = config->tile_rows > 0 ? config->tile_rows : std::max(128, kTileBlock / op->physical_tpr);
     require(op->tile_rows % 16 == 0 && op->tile_rows <= 16384, "tile_rows must be a multiple of 16, at most 16384");
-    op->tile_nnz = config->tile_nnz > 0 ? config->tile_nnz : 4096;
+    op->tile_nnz = config->tile_nnz > 0 ? config->tile_nnz : 8192;
     op->stages = config->stages > 0 ? config->stages : 2;
     require(op->stages >= 1 && op->stages <= kMaxStages, "stages must be 0 or 1..4");
-    int shared_limit = 0, multiprocessors = 0;
+    int shared_limit = 0, multiprocessors = 0, per_sm = 0;
     cuda_check(cudaDeviceGetAttribute(&shared_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, op->device), "device attribute");
     cuda_check(cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, op->device), "device attribute");
-    // default tile: the largest multiple of 256 nonzeros, up to 4096, whose buffers let two CTAs share a
-    // multiprocessor (the register budget of k_spmv_tiles is sized for two)
-    if (config->tile_nnz == 0) {
-      int per_sm = 0;
-      cuda_check(cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, op->device), "device attribute");
-      const int budget = per_sm / 2 - 1024 - 1024;   // per CTA: minus the reserved and static shared memory
-      while (op->tile_nnz > 256 && tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages) > budget)
-        op->tile_nnz -= 256;
-    }
+    cuda_check(cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, op->device), "device attribute");
     require(config->schedule >= SPMV_SCHEDULE_AUTO && config->schedule <= SPMV_SCHEDULE_CLASSES,
             "schedule must be SPMV_SCHEDULE_AUTO, _TILES or _CLASSES");
     op->schedule = config->schedule != SPMV_SCHEDULE_AUTO ? config->schedule
                                                           : (skewed_rows(m) ? SPMV_SCHEDULE_CLASSES : SPMV_SCHEDULE_TILES);
-    const int smem = tile_smem_bytes(op->tile_nnz, op->tile_rows, value_bytes, layout, op->stages);
-    if (op->schedule == SPMV_SCHEDULE_TILES && smem > shared_limit)
-      fail(SPMV_ERR_INVALID_ARGUMENT, "tiles need " + std::to_string(smem) + " bytes of shared memory, above the " +
-                                          std::to_string(shared_limit) + " a block may have");
 
     // encoded streams
     const size_t nnz = (size_t)m.nnz();
@@ -418,9 +409,36 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
       return;
     }
 
-    // tile plan
-    const TilePlan plan = plan_tiles(m, op->tile_nnz, op->tile_rows, layout == SPMV_LAYOUT_LP ? row_word.data() : nullptr,
-                                     layout == SPMV_LAYOUT_LP ? row_width.data() : nullptr);
+    // tile plan. Default tile: at most the nonzeros of tile_rows average rows (+1/8, a multiple of 256, up
+    // to 8192; a tile holds at most tile_rows rows), and small enough that the buffers let as many CTAs
+    // share a multiprocessor as its registers allow; a CSR-lp buffer holds the longest tile's words, so
+    // its size follows the plan.
+    const bool packed = layout == SPMV_LAYOUT_LP;
+    if (config->tile_nnz == 0) {
+      const double row_nnz = (double)op->tile_rows * std::max(1.0, mean_length) * 1.125;
+      op->tile_nnz = std::max(256, std::min(8192, ((int)row_nnz + 255) / 256 * 256));
+    }
+    const int register_ctas = std::max(1, tiles_occupancy(dtype, layout, tpr, op->physical_tpr, 0));
+    const int budget = per_sm / register_ctas - 1024 - 1024;   // per CTA: minus reserved and static shared memory
+    auto plan_for = [&](int tile_nnz) {
+      return plan_tiles(m, tile_nnz, op->tile_rows, packed ? row_word.data() : nullptr, packed ? row_width.data() : nullptr);
+    };
+    auto smem_for = [&](int tile_nnz, const TilePlan* plan) {
+      return tile_smem_bytes(tile_nnz, op->tile_rows, value_bytes, layout, op->stages, plan ? plan->index_words : 0);
+    };
+    if (config->tile_nnz == 0 && !packed)
+      while (op->tile_nnz > 256 && smem_for(op->tile_nnz, nullptr) > budget) op->tile_nnz -= 256;
+    TilePlan plan = plan_for(op->tile_nnz);
+    if (config->tile_nnz == 0 && packed)
+      while (op->tile_nnz > 256 && smem_for(op->tile_nnz, &plan) > budget) {
+        op->tile_nnz -= 256;
+        plan = plan_for(op->tile_nnz);
+      }
+    op->tile_index_words = plan.index_words;
+    const int smem = smem_for(op->tile_nnz, &plan);
+    if (smem > shared_limit)
+      fail(SPMV_ERR_INVALID_ARGUMENT, "tiles need " + std::to_string(smem) + " bytes of shared memory, above the " +
+                                          std::to_string(shared_limit) + " a block may have");
     op->tile_count = (int64_t)plan.tiles.size();
     op->long_count = (int64_t)plan.long_rows.size();
     op->tiles = device_upload<int4>(plan.tiles.data(), plan.tiles.size(), op->device_bytes);
@@ -430,7 +448,6 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     // long rows: one CTA per row at a time; a chunk of a long row (values, gathered x and, for CSR-lp,
     // decoded columns) lives in the CTA's shared memory, at least kTileBlock entries, at most 8192, and
     // the launch gets the larger of the tile buffers and one chunk
-    const bool packed = layout == SPMV_LAYOUT_LP;
     op->long_chunk = std::max(kTileBlock, std::min(8192, (smem / long_smem_bytes(1, value_bytes, packed)) / kTileBlock * kTileBlock));
     op->smem_bytes = std::max(smem, op->long_count > 0 ? long_smem_bytes(op->long_chunk, value_bytes, packed) : 0);
     if (op->smem_bytes > shared_limit) fail(SPMV_ERR_INVALID_ARGUMENT, "long-row chunk exceeds the shared memory of a block");
