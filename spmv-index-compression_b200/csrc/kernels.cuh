@@ -562,15 +562,13 @@ __device__ __forceinline__ void issue_tile(const KernelArgs& a, int64_t tile_id,
 
 // ---- rows longer than a tile ----------------------------------------------------------------------------
 // A row of the long-row list takes a whole CTA, chunk by chunk (a chunk starts at a multiple of T within
-// the row, so an entry keeps its lane), with the warps specialised: warps 1..7 produce, warp 0 consumes.
-// Producers fill one of two shared-memory buffers per chunk with the chunk's values and x gathered at
-// its columns (CSR-lp: first the T lane owners among them decode their lanes' columns for the chunk);
-// the consumer's T lane owners add the chunk into their lane sums in order, while the producers fill the
-// other buffer. Named barriers hand the buffers over: 1 + b "buffer b full", 3 + b "buffer b free", 5 the
-// producers' decode. Every thread walks the same rows and chunks, so every barrier completes. The lane
-// sums finish in the width-T shuffle tree of warp 0.
-constexpr int kLongProducers = kTileBlock - 32;
-
+// the row, so an entry keeps its lane), with the warps specialised. Warp 0 consumes: its T lane owners
+// add a chunk into their lane sums in order. The gatherers (warps 1..7; warps 2..7 for CSR-lp) fill one of
+// two shared-memory buffers per chunk with the chunk's values and x gathered at its columns. For CSR-lp,
+// warp 1 decodes: its T lane owners decode their lanes' columns of the chunk into one of two column
+// buffers, a chunk ahead of the gatherers. Named barriers hand the buffers over (ids 1..8, see below);
+// every thread walks the same rows and chunks, so every barrier completes. The lane sums finish in the
+// width-T shuffle tree of warp 0.
 __host__ __device__ inline int long_smem_bytes(int chunk, int value_bytes, bool packed) {
   return 4 * chunk * value_bytes + (packed ? 8 * chunk : 0);
 }
@@ -584,19 +582,16 @@ template <int ID, int THREADS>
 __device__ __forceinline__ void named_barrier_arrive() {
   asm volatile("barrier.arrive %0, %1;" ::"n"(ID), "n"(THREADS) : "memory");
 }
-// buffer b of a long-row CTA: full (producers arrive, the consumer waits) and free (the reverse)
-__device__ __forceinline__ void long_full_sync(int b) {
-  if (b == 0) named_barrier_sync<1, kTileBlock>(); else named_barrier_sync<2, kTileBlock>();
-}
-__device__ __forceinline__ void long_full_arrive(int b) {
-  if (b == 0) named_barrier_arrive<1, kTileBlock>(); else named_barrier_arrive<2, kTileBlock>();
-}
-__device__ __forceinline__ void long_free_sync(int b) {
-  if (b == 0) named_barrier_sync<3, kTileBlock>(); else named_barrier_sync<4, kTileBlock>();
-}
-__device__ __forceinline__ void long_free_arrive(int b) {
-  if (b == 0) named_barrier_arrive<3, kTileBlock>(); else named_barrier_arrive<4, kTileBlock>();
-}
+// A pair of named barriers (ids ID0 for buffer 0, ID0 + 1 for buffer 1) between THREADS threads.
+template <int ID0, int THREADS>
+struct BarrierPair {
+  __device__ static __forceinline__ void sync(int b) {
+    if (b == 0) named_barrier_sync<ID0, THREADS>(); else named_barrier_sync<ID0 + 1, THREADS>();
+  }
+  __device__ static __forceinline__ void arrive(int b) {
+    if (b == 0) named_barrier_arrive<ID0, THREADS>(); else named_barrier_arrive<ID0 + 1, THREADS>();
+  }
+};
 
 template <class V, int LAYOUT, int T>
 __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* smem, int64_t block, int64_t blocks) {
@@ -605,81 +600,91 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
   using Index = typename LayoutTraits<LAYOUT>::Index;
   constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
   constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
+  constexpr int kFirstGatherer = kPacked ? 64 : 32;          // warp 1 decodes for CSR-lp
+  constexpr int kGatherers = kTileBlock - kFirstGatherer;
+  using Full = BarrierPair<1, kGatherers + 32>;              // gatherers arrive, the consumer waits
+  using Free = BarrierPair<3, kGatherers + 32>;              // the consumer arrives, gatherers wait
+  using Decoded = BarrierPair<5, kGatherers + 32>;           // CSR-lp: the decoder arrives, gatherers wait
+  using Read = BarrierPair<7, kGatherers + 32>;              // CSR-lp: gatherers arrive, the decoder waits
   const int chunk = a.long_chunk;   // entries per chunk: a multiple of kTileBlock (and so of T)
   if (long_smem_bytes(chunk, (int)sizeof(V), kPacked) > a.smem_bytes) {   // never by construction
     if (threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusSmem);
     return;
   }
-  V* const s_values = reinterpret_cast<V*>(smem);            // [2][chunk]
-  V* const s_x = s_values + 2 * chunk;                        // [2][chunk]
-  int* const s_columns = reinterpret_cast<int*>(s_x + 2 * chunk);   // CSR-lp: [2][chunk]
+  V* const s_values = reinterpret_cast<V*>(smem);                    // [2][chunk]
+  V* const s_x = s_values + 2 * chunk;                                // [2][chunk]
+  int* const s_columns = reinterpret_cast<int*>(s_x + 2 * chunk);     // CSR-lp: [2][chunk]
   const V* values = static_cast<const V*>(a.values);
   const V* x = static_cast<const V*>(a.x);
   const Index* index = static_cast<const Index*>(a.columns);
-  const bool consumer = threadIdx.x < 32;
-  const int lane = threadIdx.x;                 // consumer: lane owner when < T
-  const int producer = (int)threadIdx.x - 32;   // producers: 0..kLongProducers-1, lane owner when < T
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   for (int64_t item = block; item < a.row_count; item += blocks) {
     const int row = a.row_list[item];
     const int64_t begin = a.row_ptr[row], length = a.row_ptr[row + 1] - begin;
     const int chunks = (int)((length + chunk - 1) / chunk);
-    if (consumer) {
+    auto count_of = [&](int k) {
+      return (int)(length - (int64_t)k * chunk < chunk ? length - (int64_t)k * chunk : chunk);
+    };
+    if (warp == 0) {   // consumer
       Acc sum = Acc(0);
       for (int k = 0; k < chunks; ++k) {
-        const int b = k & 1;
-        const int count = (int)(length - (int64_t)k * chunk < chunk ? length - (int64_t)k * chunk : chunk);
-        long_full_sync(b);
+        const int b = k & 1, count = count_of(k);
+        Full::sync(b);
         if (lane < T) {
           const V* v = s_values + b * chunk;
           const V* g = s_x + b * chunk;
 #pragma unroll 8
           for (int i = lane; i < count; i += T) sum = VT::fma(VT::widen(v[i]), VT::widen(g[i]), sum);
         }
-        long_free_arrive(b);
+        Free::arrive(b);
       }
 #pragma unroll
       for (int offset = T / 2; offset > 0; offset >>= 1) sum = VT::add(sum, __shfl_down_sync(0xffffffffu, sum, offset, T));
       if (lane == 0) static_cast<V*>(a.y)[row] = VT::narrow(sum);
-    } else {
-      const int base = kBase ? a.row_base[row] : 0;
-      // CSR-lp lane state (lane owners among the producers): the next delta's bit and the running column
+    } else if (kPacked && warp == 1) {   // CSR-lp decoder
       const int quotient = (int)(length / T), remainder = (int)(length - (int64_t)quotient * T);
-      const uint32_t width = kPacked ? a.row_width[row] : 0u;
+      const uint32_t width = a.row_width[row];
       const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
-      const uint32_t* words = kPacked ? a.words + a.row_word[row] : nullptr;
-      uint64_t bit = kPacked && producer < T
-                         ? (uint64_t)width * (uint64_t)(producer * quotient + (producer < remainder ? producer : remainder))
-                         : 0;
-      int column = base;
+      const uint32_t* words = a.words + a.row_word[row];
+      uint64_t bit = lane < T ? (uint64_t)width * (uint64_t)(lane * quotient + (lane < remainder ? lane : remainder)) : 0;
+      int column = a.row_base[row];
       for (int k = 0; k < chunks; ++k) {
-        const int b = k & 1;
-        const int count = (int)(length - (int64_t)k * chunk < chunk ? length - (int64_t)k * chunk : chunk);
-        if (k >= 2) long_free_sync(b);   // the consumer is done with chunk k - 2
+        const int b = k & 1, count = count_of(k);
+        if (k >= 2) Read::sync(b);   // the gatherers are done with the columns of chunk k - 2
         int* columns = s_columns + b * chunk;
-        if constexpr (kPacked) {
-          if (producer < T) {
-            for (int i = producer; i < count; i += T, bit += width) {
-              const uint64_t w = bit >> 5;
-              column += (int)(__funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1), (uint32_t)(bit & 31)) & mask);
-              columns[i] = column;
-            }
+        if (lane < T) {
+          for (int i = lane; i < count; i += T, bit += width) {
+            const uint64_t w = bit >> 5;
+            column += (int)(__funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1), (uint32_t)(bit & 31)) & mask);
+            columns[i] = column;
           }
-          named_barrier_sync<5, kLongProducers>();
         }
+        Decoded::arrive(b);
+      }
+      for (int k = chunks >= 2 ? chunks - 2 : 0; k < chunks; ++k) Read::sync(k & 1);
+    } else {   // gatherers
+      const int gatherer = (int)threadIdx.x - kFirstGatherer;
+      const int base = kBase ? a.row_base[row] : 0;
+      for (int k = 0; k < chunks; ++k) {
+        const int b = k & 1, count = count_of(k);
+        if (k >= 2) Free::sync(b);   // the consumer is done with chunk k - 2
+        const int* columns = s_columns + b * chunk;
+        if constexpr (kPacked) Decoded::sync(b);
         const int64_t first = begin + (int64_t)k * chunk;
         V* v = s_values + b * chunk;
         V* g = s_x + b * chunk;
 #pragma unroll 8
-        for (int i = producer; i < count; i += kLongProducers) {
+        for (int i = gatherer; i < count; i += kGatherers) {
           const int c = kPacked ? columns[i] : base + (int)load_readonly(index + first + i);
           v[i] = load_readonly(values + first + i);
           g[i] = load_readonly(x + c);
         }
-        long_full_arrive(b);
+        if constexpr (kPacked) Read::arrive(b);
+        Full::arrive(b);
       }
       // the next row refills the buffers: wait until the consumer has released the last ones
-      for (int k = chunks >= 2 ? chunks - 2 : 0; k < chunks; ++k) long_free_sync(k & 1);
+      for (int k = chunks >= 2 ? chunks - 2 : 0; k < chunks; ++k) Free::sync(k & 1);
     }
   }
 }
