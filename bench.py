@@ -342,11 +342,13 @@ def run_ours(args, rank, world, local_rank):
                    "physical_tpr": info.physical_tpr, "tile_nnz": info.tile_nnz, "rows": rows, "cols": cols,
                    "nnz": total_nnz, "parallelism": f"row shards x{world} (nnz-balanced, x replicated)",
                    "l2": f"no flush: working set {algorithmic_bytes * world / 1e9:.2f} GB > 126 MB L2",
-                   "tiles": info.tiles, "long_rows": info.long_rows},
+                   "schedule": "classes" if info.schedule == spmv.SCHEDULE_CLASSES else "tiles",
+                   "tiles": info.tiles, "listed_rows": info.listed_rows, "long_rows": info.long_rows},
         "effective_gbs": round(achieved_gbs * world, 1),
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved_gbs / peak, 4), "traffic": traffic, "peak_source": peak_source,
-                     "kernel": "k_spmv_tiles", "algorithmic_bytes_per_launch": algorithmic_bytes},
+                     "kernel": "k_spmv_classes" if info.schedule == spmv.SCHEDULE_CLASSES else "k_spmv_tiles",
+                     "algorithmic_bytes_per_launch": algorithmic_bytes},
         "clocks": clocks,
         "e2e": {"value": round(e2e_value, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": cols * value_bytes * world,
                 "d2h_bytes_per_step": rows * value_bytes, "steps": e2e_steps},
@@ -375,7 +377,9 @@ def sweep(args, torch, spmv, matrix, dtype_code, torch_dtype, x, stream):
                 continue
             with spmv.Operator(matrix, layout, dtype_code, tpr) as op:
                 ms, batch = protocol_median_ms(torch, stream, lambda: op.run(x.data_ptr(), y.data_ptr(), stream.cuda_stream))
-                entry.update(status="ok", physical_tpr=op.info().physical_tpr, t_ms=round(ms, 6), batch=batch,
+                entry.update(status="ok", physical_tpr=op.info().physical_tpr, tile_nnz=op.info().tile_nnz,
+                             schedule="classes" if op.info().schedule == spmv.SCHEDULE_CLASSES else "tiles",
+                             t_ms=round(ms, 6), batch=batch,
                              gflops=round(2.0 * matrix.nnz / (ms * 1e-3) / 1e9, 2),
                              gbs=round(memory.total / (ms * 1e-3) / 1e9, 1),
                              frac=round(memory.total / (ms * 1e-3) / 1e9 / peak, 4))
