@@ -200,10 +200,10 @@ __device__ __forceinline__ bool mbarrier_wait_bounded(uint32_t bar, uint32_t par
 }
 
 // 1-D bulk copy global -> shared (TMA), completing on the mbarrier with its byte count.
-__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
       : "memory");
 }
 
@@ -214,6 +214,69 @@ __device__ __forceinline__ T load_readonly(const T* pointer) {
 template <>
 __device__ __forceinline__ uint8_t load_readonly<uint8_t>(const uint8_t* pointer) {
   return (uint8_t)__ldg(reinterpret_cast<const unsigned char*>(pointer));
+}
+
+// L2 policies: x, gathered at random and reused across rows, is kept (evict_last); the matrix streams, read
+// once per product, leave L2 first (evict_first), so that they do not push x out.
+__device__ __forceinline__ uint64_t l2_keep_policy() {
+  uint64_t policy;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+__device__ __forceinline__ uint64_t l2_stream_policy() {
+  uint64_t policy;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
+// A read-only load of x with an L2 cache policy.
+template <class T> __device__ __forceinline__ T load_x(const T* pointer, uint64_t policy);
+template <>
+__device__ __forceinline__ double load_x<double>(const double* pointer, uint64_t policy) {
+  double value;
+  asm("ld.global.nc.L2::cache_hint.f64 %0, [%1], %2;" : "=d"(value) : "l"(pointer), "l"(policy));
+  return value;
+}
+template <>
+__device__ __forceinline__ float load_x<float>(const float* pointer, uint64_t policy) {
+  float value;
+  asm("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(value) : "l"(pointer), "l"(policy));
+  return value;
+}
+template <>
+__device__ __forceinline__ __half load_x<__half>(const __half* pointer, uint64_t policy) {
+  unsigned short bits;
+  asm("ld.global.nc.L2::cache_hint.b16 %0, [%1], %2;" : "=h"(bits) : "l"(pointer), "l"(policy));
+  return __ushort_as_half(bits);
+}
+
+// A read-only load of a matrix stream element with an L2 cache policy (values and column indices).
+template <class T> __device__ __forceinline__ T load_stream(const T* pointer, uint64_t policy) {
+  return load_x(pointer, policy);
+}
+template <>
+__device__ __forceinline__ int load_stream<int>(const int* pointer, uint64_t policy) {
+  int value;
+  asm("ld.global.nc.L2::cache_hint.b32 %0, [%1], %2;" : "=r"(value) : "l"(pointer), "l"(policy));
+  return value;
+}
+template <>
+__device__ __forceinline__ uint32_t load_stream<uint32_t>(const uint32_t* pointer, uint64_t policy) {
+  uint32_t value;
+  asm("ld.global.nc.L2::cache_hint.b32 %0, [%1], %2;" : "=r"(value) : "l"(pointer), "l"(policy));
+  return value;
+}
+template <>
+__device__ __forceinline__ uint16_t load_stream<uint16_t>(const uint16_t* pointer, uint64_t policy) {
+  unsigned short value;
+  asm("ld.global.nc.L2::cache_hint.b16 %0, [%1], %2;" : "=h"(value) : "l"(pointer), "l"(policy));
+  return value;
+}
+template <>
+__device__ __forceinline__ uint8_t load_stream<uint8_t>(const uint8_t* pointer, uint64_t policy) {
+  unsigned int value;
+  asm("ld.global.nc.L2::cache_hint.u8 %0, [%1], %2;" : "=r"(value) : "l"(pointer), "l"(policy));
+  return (uint8_t)value;
 }
 
 // The 16-byte-aligned superset of elements [first, last) of a padded stream: its global start, bytes, and
@@ -349,13 +412,14 @@ template <class V, int LAYOUT>
 struct GlobalView {
   using Index = typename LayoutTraits<LAYOUT>::Index;
   const KernelArgs& a;
-  __device__ __forceinline__ explicit GlobalView(const KernelArgs& args) : a(args) {}
+  uint64_t stream;
+  __device__ __forceinline__ explicit GlobalView(const KernelArgs& args) : a(args), stream(l2_stream_policy()) {}
   __device__ __forceinline__ int row_ptr(int row) const { return load_readonly(a.row_ptr + row); }
   __device__ __forceinline__ int row_base(int row) const { return load_readonly(a.row_base + row); }
   __device__ __forceinline__ int row_word(int row) const { return load_readonly(a.row_word + row); }
   __device__ __forceinline__ uint32_t row_width(int row) const { return load_readonly(a.row_width + row); }
-  __device__ __forceinline__ V value(int entry) const { return load_readonly(static_cast<const V*>(a.values) + entry); }
-  __device__ __forceinline__ Index index(int entry) const { return load_readonly(static_cast<const Index*>(a.columns) + entry); }
+  __device__ __forceinline__ V value(int entry) const { return load_stream(static_cast<const V*>(a.values) + entry, stream); }
+  __device__ __forceinline__ Index index(int entry) const { return load_stream(static_cast<const Index*>(a.columns) + entry, stream); }
   __device__ __forceinline__ uint32_t word(int64_t w) const { return load_readonly(a.words + w); }
 };
 
@@ -383,6 +447,7 @@ __device__ __forceinline__ typename ValueTraits<V>::Acc row_product(const View& 
   constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
   constexpr int S = T / P;
   constexpr int R = S >= kBatch ? 1 : kBatch / S;
+  const uint64_t keep = l2_keep_policy();
   Acc acc[S];
 #pragma unroll
   for (int j = 0; j < S; ++j) acc[j] = Acc(0);
@@ -396,7 +461,7 @@ __device__ __forceinline__ typename ValueTraits<V>::Acc row_product(const View& 
 #pragma unroll
           for (int j = 0; j < S; ++j) {
             const int e = entry + r * T + j * P;
-            if (e < entry_end) xv[r][j] = load_readonly(x + base + (int)view.index(e));
+            if (e < entry_end) xv[r][j] = load_x(x + base + (int)view.index(e), keep);
           }
 #pragma unroll
         for (int r = 0; r < R; ++r)
@@ -428,7 +493,7 @@ __device__ __forceinline__ typename ValueTraits<V>::Acc row_product(const View& 
             if (round + r < quotient + (lane < remainder ? 1 : 0)) {
               const uint32_t delta = (uint32_t)(lane * quotient + (lane < remainder ? lane : remainder) + round + r);
               column[j] += (int)packed_delta(view, w0, delta * width, mask);
-              xv[r][j] = load_readonly(x + column[j]);
+              xv[r][j] = load_x(x + column[j], keep);
             }
           }
 #pragma unroll
@@ -465,6 +530,7 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
   const TileView<V, LAYOUT> tile(stage, plan);
   const V* x = static_cast<const V*>(a.x);
   V* y = static_cast<V*>(a.y);
+  const uint64_t keep = l2_keep_policy();
   const int group = threadIdx.x / P, p = threadIdx.x % P;
 
   for (int first = 0; first < tile.rows; first += kGroups) {
@@ -489,7 +555,7 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
 #pragma unroll
             for (int j = 0; j < S; ++j) {
               const int e = entry + r * T + j * P;
-              if (e < entry_end) xv[r][j] = load_readonly(x + base + (int)tile.index(e));
+              if (e < entry_end) xv[r][j] = load_x(x + base + (int)tile.index(e), keep);
             }
 #pragma unroll
           for (int r = 0; r < R; ++r)
@@ -531,6 +597,7 @@ __device__ __forceinline__ void issue_tile(const KernelArgs& a, int64_t tile_id,
     index_last = (int64_t)words.y + 1;    // a window reads one word past the row's last
   }
   const AlignedRange<Index> index(index_base, index_first, index_last);
+  const uint64_t stream = l2_stream_policy();
   int* header = reinterpret_cast<int*>(stage + plan.header);
   header[0] = tile.x;
   header[1] = tile.y - tile.x;
@@ -545,19 +612,19 @@ __device__ __forceinline__ void issue_tile(const KernelArgs& a, int64_t tile_id,
   mbarrier_arrive_expect_tx(full, bytes);
   // a range may be empty (a tile of empty rows has no values): no copy is issued for 0 bytes
   if (row_ptr.bytes)
-    bulk_copy_g2s(smem_address(stage + plan.row_ptr), reinterpret_cast<const void*>(row_ptr.begin), row_ptr.bytes, full);
+    bulk_copy_g2s(smem_address(stage + plan.row_ptr), reinterpret_cast<const void*>(row_ptr.begin), row_ptr.bytes, full, stream);
   if (kBase && row_base.bytes)
-    bulk_copy_g2s(smem_address(stage + plan.row_base), reinterpret_cast<const void*>(row_base.begin), row_base.bytes, full);
+    bulk_copy_g2s(smem_address(stage + plan.row_base), reinterpret_cast<const void*>(row_base.begin), row_base.bytes, full, stream);
   if (kPacked && row_base.bytes) {
     const AlignedRange<int> row_word(a.row_word, tile.x, tile.y);
-    bulk_copy_g2s(smem_address(stage + plan.row_word), reinterpret_cast<const void*>(row_word.begin), row_word.bytes, full);
+    bulk_copy_g2s(smem_address(stage + plan.row_word), reinterpret_cast<const void*>(row_word.begin), row_word.bytes, full, stream);
   }
   if (kPacked && row_width.bytes)
-    bulk_copy_g2s(smem_address(stage + plan.row_width), reinterpret_cast<const void*>(row_width.begin), row_width.bytes, full);
+    bulk_copy_g2s(smem_address(stage + plan.row_width), reinterpret_cast<const void*>(row_width.begin), row_width.bytes, full, stream);
   if (values.bytes)
-    bulk_copy_g2s(smem_address(stage + plan.values), reinterpret_cast<const void*>(values.begin), values.bytes, full);
+    bulk_copy_g2s(smem_address(stage + plan.values), reinterpret_cast<const void*>(values.begin), values.bytes, full, stream);
   if (index.bytes)
-    bulk_copy_g2s(smem_address(stage + plan.index), reinterpret_cast<const void*>(index.begin), index.bytes, full);
+    bulk_copy_g2s(smem_address(stage + plan.index), reinterpret_cast<const void*>(index.begin), index.bytes, full, stream);
 }
 
 // ---- rows longer than a tile ----------------------------------------------------------------------------
@@ -666,6 +733,7 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
     } else {   // gatherers
       const int gatherer = (int)threadIdx.x - kFirstGatherer;
       const int base = kBase ? a.row_base[row] : 0;
+      const uint64_t keep = l2_keep_policy(), stream = l2_stream_policy();
       for (int k = 0; k < chunks; ++k) {
         const int b = k & 1, count = count_of(k);
         if (k >= 2) Free::sync(b);   // the consumer is done with chunk k - 2
@@ -676,9 +744,9 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
         V* g = s_x + b * chunk;
 #pragma unroll 8
         for (int i = gatherer; i < count; i += kGatherers) {
-          const int c = kPacked ? columns[i] : base + (int)load_readonly(index + first + i);
-          v[i] = load_readonly(values + first + i);
-          g[i] = load_readonly(x + c);
+          const int c = kPacked ? columns[i] : base + (int)load_stream(index + first + i, stream);
+          v[i] = load_stream(values + first + i, stream);
+          g[i] = load_x(x + c, keep);
         }
         if constexpr (kPacked) Read::arrive(b);
         Full::arrive(b);
@@ -718,6 +786,7 @@ __device__ __forceinline__ void short_rows(const KernelArgs& a, int64_t chunk) {
   const GlobalView<V, LAYOUT> g(a);
   const V* x = static_cast<const V*>(a.x);
   V* y = static_cast<V*>(a.y);
+  const uint64_t keep = l2_keep_policy();
   int row[U], begin[U], length[U];
   bool mine[U];
 #pragma unroll
@@ -736,7 +805,7 @@ __device__ __forceinline__ void short_rows(const KernelArgs& a, int64_t chunk) {
       const int base = kBase && mine[u] ? g.row_base(row[u]) : 0;
 #pragma unroll
       for (int j = 0; j < kShortMax; ++j)
-        if (mine[u] && j < length[u]) xv[u][j] = load_readonly(x + base + (int)g.index(begin[u] + j));
+        if (mine[u] && j < length[u]) xv[u][j] = load_x(x + base + (int)g.index(begin[u] + j), keep);
     } else {
       if (mine[u] && length[u] > 0) {
         const int quotient = length[u] / T, remainder = length[u] - quotient * T;
@@ -753,7 +822,7 @@ __device__ __forceinline__ void short_rows(const KernelArgs& a, int64_t chunk) {
           if (j < length[u]) {
             const uint32_t delta = (uint32_t)(lane * quotient + (lane < remainder ? lane : remainder) + k);
             column[lane] += (int)packed_delta(g, w0, delta * width, mask);
-            xv[u][j] = load_readonly(x + column[lane]);
+            xv[u][j] = load_x(x + column[lane], keep);
           }
         }
       }
