@@ -334,6 +334,10 @@ def run_ours(args, rank, world, local_rank):
         return
     peak, peak_source = measured_peak()
     traffic = profiled_traffic(args.workload, args.layout, args.tpr)
+    # x gathers: one per nonzero; against the measured rate of random single-element gathers from an
+    # array the size of x (the ceiling for scattered columns, where each element costs a 32-byte sector)
+    gather_ceiling = spmv.gather_rate(cols, value_bytes, 10)
+    gather_rate = total_nnz / (ms_per_step * 1e-3)
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
@@ -349,6 +353,11 @@ def run_ours(args, rank, world, local_rank):
                      "frac": round(achieved_gbs / peak, 4), "traffic": traffic, "peak_source": peak_source,
                      "kernel": "k_spmv_classes" if info.schedule == spmv.SCHEDULE_CLASSES else "k_spmv_tiles",
                      "algorithmic_bytes_per_launch": algorithmic_bytes},
+        "x_gathers": {"per_step": total_nnz, "achieved_per_s": round(gather_rate, 1),
+                      "random_gather_ceiling_per_s": round(gather_ceiling, 1),
+                      "frac": round(gather_rate / gather_ceiling, 4),
+                      "note": "ceiling measured by spmv_gather_rate on an array of cols elements; above 1 means the "
+                              "gathers reuse L1/L2 lines"},
         "clocks": clocks,
         "e2e": {"value": round(e2e_value, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": cols * value_bytes * world,
                 "d2h_bytes_per_step": rows * value_bytes, "steps": e2e_steps},

@@ -268,6 +268,11 @@ int spmv_launch(int layout, int dtype, int tpr, const spmv_device_matrix* matrix
  * `bytes`-byte device buffer (16-byte vector loads, no reuse), over `reps` timed passes after 3 warm-ups,
  * on the current device. The roof of the reference's epsilon. */
 int spmv_read_bandwidth(int64_t bytes, int reps, double* gigabytes_per_second);
+/* The ceiling of random x gathers: the median rate (elements per second) of reads of single elements of
+ * value_bytes (2, 4 or 8) at pseudo-random positions of an array of `elements` elements, with every
+ * multiprocessor busy. No counterpart in the reference (its roofline is the streaming read above); it
+ * bounds SpMV on matrices whose columns are scattered, where each x element costs a 32-byte sector. */
+int spmv_gather_rate(int64_t elements, int value_bytes, int reps, double* elements_per_second);
 
 /* ---- synthetic matrices for the benchmark configurations ---------------------------------------- */
 /* 2D 5-point Laplacian on grid x grid (diagonal 4, neighbours -1). */

@@ -605,8 +605,76 @@ __global__ void __launch_bounds__(512) k_read_stream(const uint4* __restrict__ s
   if (accumulator == 0x9e3779b9u) *sink = accumulator;   // practically never: keeps the loads alive
 }
 
+// Random gathers: every thread reads 16 elements at hashed positions (an integer mix, in bounds by the
+// power-of-two mask) and folds them into a hash only to stop the loads being dropped.
+__device__ __forceinline__ uint32_t gather_position(uint32_t value) {
+  value ^= value >> 16;
+  value *= 0x7feb352du;
+  value ^= value >> 15;
+  value *= 0x846ca68bu;
+  return value ^ (value >> 16);
+}
+
+template <class E>
+__global__ void __launch_bounds__(256) k_gather_random(const E* __restrict__ source, uint32_t mask, uint32_t seed, unsigned* sink) {
+  const uint32_t thread = blockIdx.x * blockDim.x + threadIdx.x;
+  E values[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) values[k] = __ldg(source + (gather_position(thread * 16 + k + seed) & mask));
+  unsigned folded = 0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) folded = folded * 0x01000193u ^ (unsigned)values[k];   // can take any value
+  if (folded == 0x9e3779b9u) *sink = folded;   // practically never: keeps the loads alive
+}
+
 }  // namespace
 }  // namespace spmvb200
+
+
+extern "C" int spmv_gather_rate(int64_t elements, int value_bytes, int reps, double* elements_per_second) {
+  return guarded([&] {
+    require(elements_per_second && reps >= 1 && elements >= 1024 && elements <= (1LL << 31) &&
+                (value_bytes == 2 || value_bytes == 4 || value_bytes == 8),
+            "bad arguments");
+    int64_t size = 1;
+    while (size * 2 <= elements) size *= 2;   // a power of two, so that the mask keeps positions in bounds
+    void* buffer = nullptr;
+    unsigned* sink = nullptr;
+    cuda_check(cudaMalloc(&buffer, (size_t)size * value_bytes), "cudaMalloc");
+    cudaError_t status = cudaMalloc(&sink, sizeof(unsigned));
+    if (status == cudaSuccess) status = cudaMemset(buffer, 1, (size_t)size * value_bytes);
+    int multiprocessors = 0, device = 0;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
+    const unsigned blocks = (unsigned)multiprocessors * 8 * 32;
+    const uint32_t mask = (uint32_t)(size - 1);
+    cudaEvent_t start = nullptr, end = nullptr;
+    std::vector<float> times;
+    if (status == cudaSuccess) status = cudaEventCreate(&start);
+    if (status == cudaSuccess) status = cudaEventCreate(&end);
+    for (int rep = -3; rep < reps && status == cudaSuccess; ++rep) {
+      const uint32_t seed = (uint32_t)(rep + 3) * 0x9e3779b9u;
+      cudaEventRecord(start);
+      if (value_bytes == 2) k_gather_random<unsigned short><<<blocks, 256>>>(static_cast<unsigned short*>(buffer), mask, seed, sink);
+      else if (value_bytes == 4) k_gather_random<unsigned><<<blocks, 256>>>(static_cast<unsigned*>(buffer), mask, seed, sink);
+      else k_gather_random<unsigned long long><<<blocks, 256>>>(static_cast<unsigned long long*>(buffer), mask, seed, sink);
+      cudaEventRecord(end);
+      status = cudaGetLastError();
+      if (status == cudaSuccess) status = cudaEventSynchronize(end);
+      float ms = 0.0f;
+      if (status == cudaSuccess) status = cudaEventElapsedTime(&ms, start, end);
+      if (rep >= 0) times.push_back(ms);
+    }
+    if (start) cudaEventDestroy(start);
+    if (end) cudaEventDestroy(end);
+    cudaFree(buffer);
+    if (sink) cudaFree(sink);
+    cuda_check(status, "gather rate");
+    std::sort(times.begin(), times.end());
+    const double median = times[times.size() / 2];
+    *elements_per_second = (double)blocks * 256.0 * 16.0 / (median * 1e-3);
+  });
+}
 
 extern "C" int spmv_read_bandwidth(int64_t bytes, int reps, double* gigabytes_per_second) {
   return guarded([&] {

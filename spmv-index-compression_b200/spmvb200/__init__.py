@@ -176,6 +176,7 @@ _sig("spmv_fill_uniform", _i, _i, _i64, _u64, _v)
 _sig("spmv_fill_reference_x", _i, _i, _i64, _v)
 _sig("spmv_shard_rows", _i, _v, _i, _v)
 _sig("spmv_read_bandwidth", _i, _i64, _i, ctypes.POINTER(_d))
+_sig("spmv_gather_rate", _i, _i64, _i, _i, ctypes.POINTER(_d))
 _sig("spmv_comm_unique_id", _i, _v)
 _sig("spmv_comm_create", _i, _i, _i, _v, _i, _c_void_pp)
 _sig("spmv_comm_destroy", None, _v)
@@ -566,6 +567,14 @@ def read_bandwidth(bytes_: int = 4 << 30, reps: int = 20) -> float:
     roofline.cuh:101)."""
     result = ctypes.c_double()
     _check(_lib.spmv_read_bandwidth(bytes_, reps, ctypes.byref(result)))
+    return result.value
+
+
+def gather_rate(elements: int, value_bytes: int, reps: int = 10) -> float:
+    """Measured rate (elements/s) of random single-element reads from an array of `elements` elements of
+    value_bytes each: the ceiling of the x gathers of a matrix with scattered columns."""
+    result = ctypes.c_double()
+    _check(_lib.spmv_gather_rate(elements, value_bytes, reps, ctypes.byref(result)))
     return result.value
 
 

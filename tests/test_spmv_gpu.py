@@ -254,3 +254,13 @@ def test_read_bandwidth_is_a_device_memory_rate():
     assert 1000.0 < rate < 8200.0
     with pytest.raises(spmv.SpmvError):
         spmv.read_bandwidth(0, 5)
+
+
+def test_gather_rate_is_below_the_sector_rate():
+    """The random-gather ceiling: single 2-, 4- and 8-byte elements at random positions of a 16 MB array;
+    each costs a 32-byte L2 sector, so the rate times 32 bytes stays under 40 TB/s and above 1 TB/s."""
+    for value_bytes in (2, 4, 8):
+        rate = spmv.gather_rate((16 << 20) // value_bytes, value_bytes, 3)
+        assert 1e12 / 32 < rate < 40e12 / 32, (value_bytes, rate)
+    with pytest.raises(spmv.SpmvError):
+        spmv.gather_rate(1 << 20, 3, 3)
