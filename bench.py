@@ -37,9 +37,12 @@ WORKLOADS = {
     "laplacian": "2D 5-point Laplacian 256^2, FP64, x U[-1,1] seed 0",
     "band": "random band n=1M, half-bandwidth 2000, Poisson(32)+diagonal, FP32, seed 1",
     "powerlaw": "power law n=8M, Zipf(1.8) row lengths in [1,100000] rescaled to mean 12, FP16, seed 3",
+    "fem": "block FEM n=32M, 8x8 blocks, diagonal + 7 block-columns at offsets U[-50000,50000], FP32, seed 4; "
+           "chained products y -> x with an NCCL all-gather of y",
 }
-DTYPE_OF = {"stencil27": "fp64", "laplacian": "fp64", "band": "fp32", "powerlaw": "fp16"}
-SEED_OF = {"stencil27": 2, "laplacian": 0, "band": 1, "powerlaw": 3}
+DTYPE_OF = {"stencil27": "fp64", "laplacian": "fp64", "band": "fp32", "powerlaw": "fp16", "fem": "fp32"}
+SEED_OF = {"stencil27": 2, "laplacian": 0, "band": 1, "powerlaw": 3, "fem": 4}
+FEM_ROWS = 32_000_000
 METRIC = "SpMV GFLOP/s & HBM GB/s (vs ~8 TB/s) per layout/T at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
 
@@ -73,7 +76,16 @@ def build_matrix(spmv, workload):
         return spmv.synth_laplacian2d(256)
     if workload == "band":
         return spmv.synth_random_band(1_000_000, 2000, 32.0, 1)
+    if workload == "fem":
+        return spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, 0, FEM_ROWS)
     return spmv.synth_power_law(8_000_000, 1.8, 100_000, 12.0, 3)
+
+
+def fem_bounds(world):
+    """Row shards of the block-FEM matrix: every row has 64 nonzeros, so equal block-aligned row ranges are
+    nnz-balanced."""
+    per_rank = (FEM_ROWS // 8 + world - 1) // world * 8
+    return np.array([min(FEM_ROWS, rank * per_rank) for rank in range(world + 1)], dtype=np.int32)
 
 
 def measured_peak():
@@ -195,7 +207,10 @@ def run_reference(args, rank, world):
     import spmvb200 as spmv
     if rank != 0:
         return
-    matrix = build_matrix(spmv, args.workload)
+    if args.workload == "fem":   # a row range of the 2.05 G-nonzero matrix stands in (host memory)
+        matrix = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, 0, 2_000_000)
+    else:
+        matrix = build_matrix(spmv, args.workload)
     dtype_code = spmv.DTYPE_BY_NAME[DTYPE_OF[args.workload]]
     budget = 120.0
     rate, sample, cores = cpu_product_rate(matrix, dtype_code, args.tpr, budget, steps=args.steps, warmup=args.warmup)
@@ -245,6 +260,9 @@ def protocol_median_ms(torch, stream, body, samples=20, warmup=3, min_sample_ms=
 
 
 def run_ours(args, rank, world, local_rank):
+    if args.workload == "fem":
+        run_fem(args, rank, world, local_rank)
+        return
     import torch
     import spmvb200 as spmv
     dist = None
@@ -364,6 +382,114 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": args.steps,
     }
     line.update(extras)
+    print(json.dumps(line), flush=True)
+
+
+def run_fem(args, rank, world, local_rank):
+    """Config 5: the block-FEM matrix row-sharded over the ranks (each rank builds only its rows), a step is
+    one chained product: every rank's shard product into its slice of the next x, then the slices
+    all-gathered over NCCL (spmv_chain_run). The kernel alone is also timed for the roofline."""
+    import torch
+    import spmvb200 as spmv
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(device)
+    dtype_code = spmv.DTYPE_BY_NAME["fp32"]
+    layout = spmv.LAYOUT_BY_NAME[args.layout]
+    bounds = fem_bounds(world)
+    shard = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, int(bounds[rank]), int(bounds[rank + 1]))
+    total_nnz = 64 * FEM_ROWS
+    facts = spmv.facts_of(shard)
+    if not spmv.configuration_admissible(shard, facts, spmv.Configuration.of(layout, dtype_code, args.tpr)):
+        raise SystemExit(f"layout {args.layout} at T={args.tpr} is not admissible for fem")
+    op = spmv.Operator(shard, layout, dtype_code, args.tpr, physical_tpr=args.physical_tpr, tile_nnz=args.tile_nnz,
+                       device=local_rank)
+    info = op.info()
+    algorithmic_bytes = info.memory.total
+    del shard
+    box = [spmv.comm_unique_id() if rank == 0 else None]
+    if dist is not None:
+        dist.broadcast_object_list(box, src=0)
+    comm = spmv.Comm(world, rank, box[0], device=local_rank)
+    x_host = spmv.fill_uniform(dtype_code, FEM_ROWS, SEED_OF["fem"])
+    x_current = torch.from_numpy(x_host).to(device)
+    x_next = torch.zeros_like(x_current)
+    y_alone = torch.empty(int(bounds[rank + 1] - bounds[rank]), dtype=torch.float32, device=device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    chain = lambda count: spmv.chain_run(op, comm, bounds, x_current.data_ptr(), x_next.data_ptr(), count,  # noqa: E731
+                                         stream.cuda_stream)
+    chain(args.warmup)
+    comm.check(stream.cuda_stream, 120000)
+    barrier()
+    gpu_id = torch.cuda.get_device_properties(local_rank).uuid
+    sampler = ClockSampler(f"GPU-{gpu_id}" if not str(gpu_id).startswith("GPU-") else str(gpu_id))
+    sampler.start()
+    barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    chain(args.steps)
+    end.record(stream)
+    comm.check(stream.cuda_stream, 120000)
+    barrier()
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(end)
+    # the product kernel alone on this rank's shard (x held still), for the roofline
+    kernel_ms = event_ms(torch, stream, lambda: op.run(x_current.data_ptr(), y_alone.data_ptr(), stream.cuda_stream),
+                         max(3, min(args.steps, 50)))
+    kernel_steps = max(3, min(args.steps, 50))
+    op.check()
+    # end to end: x in from pinned host memory, one chained product, this rank's new slice of x out
+    x_pinned = torch.from_numpy(x_host).pin_memory()
+    slice_rows = int(bounds[rank + 1] - bounds[rank])
+    y_pinned = torch.empty(slice_rows, dtype=torch.float32).pin_memory()
+    e2e_steps = max(1, min(args.steps, 10))
+
+    def e2e_step():
+        x_current.copy_(x_pinned, non_blocking=True)
+        chain(1)
+        y_pinned.copy_(x_next[int(bounds[rank]):int(bounds[rank + 1])], non_blocking=True)
+    barrier()
+    e2e_ms = event_ms(torch, stream, e2e_step, e2e_steps)
+    comm.check(stream.cuda_stream, 120000)
+    barrier()
+    times = torch.tensor([elapsed_ms, kernel_ms, e2e_ms], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    elapsed_ms, kernel_ms, e2e_ms = times.tolist()
+    comm.close()
+    if rank != 0:
+        return
+    ms_per_step = elapsed_ms / args.steps
+    kernel_ms_per_launch = kernel_ms / kernel_steps
+    achieved_gbs = algorithmic_bytes / (kernel_ms_per_launch * 1e-3) / 1e9
+    peak, peak_source = measured_peak()
+    line = {
+        "metric": METRIC, "value": round(2.0 * total_nnz * args.steps / (elapsed_ms * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": WORKLOADS["fem"], "layout": args.layout, "tpr": args.tpr, "rows": FEM_ROWS,
+                   "nnz": total_nnz, "parallelism": f"row shards x{world} (block-aligned, nnz-balanced), NCCL all-gather "
+                                                   "of y between chained products",
+                   "l2": f"no flush: {algorithmic_bytes / 1e9:.2f} GB per rank > 126 MB L2",
+                   "physical_tpr": info.physical_tpr, "tile_nnz": info.tile_nnz, "tiles": info.tiles},
+        "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved_gbs / peak, 4), "traffic": None, "peak_source": peak_source,
+                     "kernel": "k_spmv_tiles", "algorithmic_bytes_per_launch": algorithmic_bytes,
+                     "kernel_ms": round(kernel_ms_per_launch, 6)},
+        "clocks": clocks,
+        "e2e": {"value": round(2.0 * total_nnz * e2e_steps / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
+                "h2d_bytes_per_step": FEM_ROWS * 4 * world, "d2h_bytes_per_step": FEM_ROWS * 4, "steps": e2e_steps},
+        "gpu_launches": args.steps,
+    }
     print(json.dumps(line), flush=True)
 
 

@@ -108,14 +108,14 @@ TilePlan plan_tiles(const Csr& matrix, int tile_nnz, int tile_rows, const int* r
   return plan;
 }
 
-// Physical threads per row P: the fewest that leave a thread at most 32 entries of an average row (one
+// Physical threads per row P: the fewest that leave a thread at most 28 entries of an average row (one
 // batch of gathers), and at least T/16 (at most 16 lane sums per thread; T/8 for CSR-lp, whose 16-lane
 // variants gather half as deep). A tile then holds 256/P rows (at least 128), so that one pass of the
-// CTA's 256/P row groups covers it. Measured on B200 (27-point stencil, FP64): P = 1 at T = 8 and P = 2
-// with 128-row tiles at T = 32 both reach about 82 % of the measured HBM peak in CSR-i32.
+// CTA's 256/P row groups covers it. Measured on B200 (CSR-i32): 27-point stencil (27 entries a row)
+// P = 1 at T = 8; random band (33) P = 2; block FEM (64) P = 4.
 int choose_physical_tpr(int tpr, int layout, double mean_length) {
   int physical = 1;
-  while (physical < tpr && mean_length / physical > 32.0) physical *= 2;
+  while (physical < tpr && mean_length / physical > 28.0) physical *= 2;
   const int max_slots = layout == SPMV_LAYOUT_LP ? 8 : 16;
   while (tpr / physical > max_slots) physical *= 2;
   return physical;
