@@ -168,6 +168,13 @@ int spmv_lane_packed_word_count(const spmv_csr* matrix, int tpr, int64_t* word_c
 /* build_packed_deltas (bench_csr_width.cu:861): row_word[rows], row_width[rows], words[word_count]. */
 int spmv_encode_lane_packed(const spmv_csr* matrix, int tpr, int64_t word_count, int* row_word, uint8_t* row_width,
                             uint32_t* words);
+/* build_packed_deltas (bench_csr_width.cu:861) on the GPU, from device-resident row_ptr (int32[rows+1])
+ * and col_ind (int32[nnz], sorted within rows): the same row_word, row_width and words as
+ * spmv_encode_lane_packed. Call with words NULL to get word_count (2 spare words included) and the row
+ * arrays; call again with words of word_capacity >= word_count to pack. Synchronises the stream. */
+int spmv_encode_lane_packed_device(const int* row_ptr, const int* col_ind, int rows, int tpr, int* row_word,
+                                   uint8_t* row_width, uint32_t* words, int64_t word_capacity, int64_t* word_count,
+                                   void* stream);
 
 /* ---- device operator: DeviceMatrix<T> + Configuration (bench_csr_width.cu:88, :128) ------------- */
 typedef struct spmv_operator spmv_operator;

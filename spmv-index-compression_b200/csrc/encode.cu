@@ -1,0 +1,206 @@
+// encode.cu — the CSR-lp encoder on the GPU: the same streams as encode_lane_packed (layouts.cpp), which
+// restates the reference's build_packed_deltas (bench_csr_width.cu:861-917), built from device-resident
+// row_ptr and col_ind.
+//
+//   1. k_lp_widths   one warp per row: the widest lane delta (from the entry T positions earlier, or from
+//                    the row's first column for the first T entries), its bit width, and the row's words;
+//   2. a scan of the words per row into row_word (block scans, a scan of the block sums, an add);
+//   3. k_lp_pack     one warp per row: every delta OR-ed into its words at bit
+//                    width * (lane * quotient + min(lane, remainder) + step), lane-major.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+
+#include "capi_internal.hpp"
+
+namespace spmvb200 {
+namespace {
+
+constexpr int kScanBlock = 1024;
+
+__global__ void k_lp_widths(const int* __restrict__ row_ptr, const int* __restrict__ col, int rows, int tpr,
+                            uint8_t* __restrict__ row_width, long long* __restrict__ row_words) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) / 32;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; row < rows; row += warps) {
+    const int begin = row_ptr[row], end = row_ptr[row + 1];
+    unsigned widest = 0;
+    for (int entry = begin + lane; entry < end; entry += 32) {
+      const int delta = entry - begin < tpr ? col[entry] - col[begin] : col[entry] - col[entry - tpr];
+      widest = max(widest, (unsigned)delta);
+    }
+    widest = __reduce_max_sync(0xffffffffu, widest);
+    if (lane == 0) {
+      const int width = widest == 0 ? 0 : 32 - __clz((int)widest);
+      row_width[row] = (uint8_t)width;
+      row_words[row] = ((long long)(end - begin) * width + 31) / 32;
+    }
+  }
+}
+
+// Exclusive scan of kScanBlock values per block; the block's total goes to sums[block].
+__global__ void __launch_bounds__(kScanBlock) k_scan_blocks(const long long* __restrict__ values, int64_t count,
+                                                          long long* __restrict__ scanned, long long* __restrict__ sums) {
+  __shared__ long long warp_totals[kScanBlock / 32];
+  const int64_t index = (int64_t)blockIdx.x * kScanBlock + threadIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+  const long long value = index < count ? values[index] : 0;
+  long long inclusive = value;
+#pragma unroll
+  for (int offset = 1; offset < 32; offset <<= 1) {
+    const long long other = __shfl_up_sync(0xffffffffu, inclusive, offset);
+    if (lane >= offset) inclusive += other;
+  }
+  if (lane == 31) warp_totals[warp] = inclusive;
+  __syncthreads();
+  if (warp == 0) {
+    long long total = warp_totals[lane];
+#pragma unroll
+    for (int offset = 1; offset < 32; offset <<= 1) {
+      const long long other = __shfl_up_sync(0xffffffffu, total, offset);
+      if (lane >= offset) total += other;
+    }
+    warp_totals[lane] = total;   // inclusive over warps
+  }
+  __syncthreads();
+  const long long before = warp == 0 ? 0 : warp_totals[warp - 1];
+  if (index < count) scanned[index] = before + inclusive - value;
+  if (threadIdx.x == kScanBlock - 1) sums[blockIdx.x] = before + inclusive;
+}
+
+// One block: the exclusive scan of `count` block sums in place, chunk by chunk with a carry, and the
+// grand total in *total.
+__global__ void __launch_bounds__(kScanBlock) k_scan_sums(long long* __restrict__ sums, int64_t count,
+                                                        long long* __restrict__ total) {
+  __shared__ long long warp_totals[kScanBlock / 32];
+  __shared__ long long carry;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int64_t first = 0; first < count; first += kScanBlock) {
+    const int64_t index = first + threadIdx.x;
+    const long long value = index < count ? sums[index] : 0;
+    long long inclusive = value;
+#pragma unroll
+    for (int offset = 1; offset < 32; offset <<= 1) {
+      const long long other = __shfl_up_sync(0xffffffffu, inclusive, offset);
+      if (lane >= offset) inclusive += other;
+    }
+    if (lane == 31) warp_totals[warp] = inclusive;
+    __syncthreads();
+    if (warp == 0) {
+      long long sum = warp_totals[lane];
+#pragma unroll
+      for (int offset = 1; offset < 32; offset <<= 1) {
+        const long long other = __shfl_up_sync(0xffffffffu, sum, offset);
+        if (lane >= offset) sum += other;
+      }
+      warp_totals[lane] = sum;
+    }
+    __syncthreads();
+    const long long before = warp == 0 ? 0 : warp_totals[warp - 1];
+    if (index < count) sums[index] = carry + before + inclusive - value;
+    __syncthreads();
+    if (threadIdx.x == kScanBlock - 1) carry += before + inclusive;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total = carry;
+}
+
+__global__ void k_scan_add(const long long* __restrict__ scanned, const long long* __restrict__ sums, int64_t count,
+                           int* __restrict__ row_word) {
+  const int64_t index = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (index < count) row_word[index] = (int)(scanned[index] + sums[index / kScanBlock]);
+}
+
+__global__ void k_lp_pack(const int* __restrict__ row_ptr, const int* __restrict__ col, int rows, int tpr,
+                          const uint8_t* __restrict__ row_width, const int* __restrict__ row_word,
+                          uint32_t* __restrict__ words) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) / 32;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; row < rows; row += warps) {
+    const int width = row_width[row];
+    if (width == 0) continue;
+    const int begin = row_ptr[row], length = row_ptr[row + 1] - begin;
+    const int quotient = length / tpr, remainder = length - quotient * tpr;
+    uint32_t* stream = words + row_word[row];
+    for (int offset = lane; offset < length; offset += 32) {
+      const int entry = begin + offset;
+      const uint32_t delta = (uint32_t)(offset < tpr ? col[entry] - col[begin] : col[entry] - col[entry - tpr]);
+      const int lane_of = offset % tpr, step = offset / tpr;
+      const int64_t bit = (int64_t)width * ((int64_t)lane_of * quotient + min(lane_of, remainder) + step);
+      const int shift = (int)(bit & 31);
+      if (delta != 0) {
+        atomicOr(stream + (bit >> 5), delta << shift);
+        if (shift + width > 32) atomicOr(stream + (bit >> 5) + 1, delta >> (32 - shift));
+      }
+    }
+  }
+}
+
+unsigned warp_blocks(int rows) {
+  const int64_t blocks = ((int64_t)rows * 32 + 255) / 256;
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks, 148 * 64));
+}
+
+}  // namespace
+
+// Row widths and row_word on the device; returns the word count including the 2 spare words. The
+// scratch (words per row, block sums, total) is allocated here.
+int64_t device_lane_packed_layout(const int* row_ptr, const int* col_ind, int rows, int tpr, int* row_word,
+                                  uint8_t* row_width, cudaStream_t stream) {
+  if (rows == 0) return 2;
+  const int64_t blocks = ((int64_t)rows + kScanBlock - 1) / kScanBlock;
+  long long* scratch = nullptr;
+  const size_t scratch_count = 2 * (size_t)rows + (size_t)blocks + 1;
+  cudaError_t status = cudaMalloc(&scratch, scratch_count * sizeof(long long));
+  if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("cudaMalloc: ") + cudaGetErrorString(status));
+  long long* row_words = scratch;
+  long long* scanned = scratch + rows;
+  long long* sums = scanned + rows;
+  long long* total = sums + blocks;
+  k_lp_widths<<<warp_blocks(rows), 256, 0, stream>>>(row_ptr, col_ind, rows, tpr, row_width, row_words);
+  k_scan_blocks<<<(unsigned)blocks, kScanBlock, 0, stream>>>(row_words, rows, scanned, sums);
+  k_scan_sums<<<1, kScanBlock, 0, stream>>>(sums, blocks, total);
+  k_scan_add<<<(unsigned)(((int64_t)rows + 255) / 256), 256, 0, stream>>>(scanned, sums, rows, row_word);
+  long long host_total = 0;
+  status = cudaGetLastError();
+  if (status == cudaSuccess) status = cudaMemcpyAsync(&host_total, total, sizeof(long long), cudaMemcpyDeviceToHost, stream);
+  if (status == cudaSuccess) status = cudaStreamSynchronize(stream);
+  cudaFree(scratch);
+  if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("CSR-lp layout on the device: ") + cudaGetErrorString(status));
+  return host_total + 2;
+}
+
+void device_lane_packed_pack(const int* row_ptr, const int* col_ind, int rows, int tpr, const int* row_word,
+                             const uint8_t* row_width, uint32_t* words, int64_t word_count, cudaStream_t stream) {
+  cudaError_t status = cudaMemsetAsync(words, 0, sizeof(uint32_t) * (size_t)word_count, stream);
+  if (status == cudaSuccess && rows > 0) {
+    k_lp_pack<<<warp_blocks(rows), 256, 0, stream>>>(row_ptr, col_ind, rows, tpr, row_width, row_word, words);
+    status = cudaGetLastError();
+  }
+  if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("CSR-lp packing on the device: ") + cudaGetErrorString(status));
+}
+
+}  // namespace spmvb200
+
+using namespace spmvb200;
+
+extern "C" int spmv_encode_lane_packed_device(const int* row_ptr, const int* col_ind, int rows, int tpr, int* row_word,
+                                              uint8_t* row_width, uint32_t* words, int64_t word_capacity,
+                                              int64_t* word_count, void* stream) {
+  return guarded([&] {
+    require(row_ptr && (col_ind || rows == 0) && row_word && row_width && word_count && rows >= 0, "bad arguments");
+    require(valid_tpr(tpr), "threads per row must be 2, 4, 8, 16 or 32");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t count = device_lane_packed_layout(row_ptr, col_ind, rows, tpr, row_word, row_width, s);
+    *word_count = count;
+    if (count - 2 > INT32_MAX) fail(SPMV_ERR_NOT_ADMISSIBLE, "CSR-lp stream exceeds 2^31 words");
+    if (words == nullptr) return;
+    require(word_capacity >= count, "words holds fewer than word_count words");
+    device_lane_packed_pack(row_ptr, col_ind, rows, tpr, row_word, row_width, words, count, s);
+    const cudaError_t status = cudaStreamSynchronize(s);
+    if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("CSR-lp packing on the device: ") + cudaGetErrorString(status));
+  });
+}

@@ -60,7 +60,31 @@ T* device_upload(const void* host, size_t count, int64_t& total_bytes) {
   return device;
 }
 
+// A device buffer owned for the duration of operator creation.
+template <class T>
+struct DeviceBuffer {
+  T* data = nullptr;
+  void allocate(size_t count, const T* host) {
+    cuda_check(cudaMalloc(reinterpret_cast<void**>(&data), sizeof(T) * std::max<size_t>(count, 1)), "cudaMalloc");
+    if (count) cuda_check(cudaMemcpy(data, host, sizeof(T) * count, cudaMemcpyHostToDevice), "upload");
+  }
+  void release() {
+    if (data) cudaFree(data);
+    data = nullptr;
+  }
+  ~DeviceBuffer() { release(); }
+};
+
+// CSR-lp matrices with at least this many nonzeros are encoded on the device.
+constexpr int64_t kDeviceEncodeNnz = 1 << 20;
+
 }  // namespace
+
+// encode.cu
+int64_t device_lane_packed_layout(const int* row_ptr, const int* col_ind, int rows, int tpr, int* row_word,
+                                  uint8_t* row_width, cudaStream_t stream);
+void device_lane_packed_pack(const int* row_ptr, const int* col_ind, int rows, int tpr, const int* row_word,
+                             const uint8_t* row_width, uint32_t* words, int64_t word_count, cudaStream_t stream);
 
 // Tile plan: maximal runs of consecutive rows with at most tile_nnz nonzeros and tile_rows rows; a row
 // with more than tile_nnz nonzeros is listed as long and processed by the vector path instead.
@@ -305,11 +329,24 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     for (int row = 0; row < m.rows; ++row)
       if (m.row_ptr[row + 1] > m.row_ptr[row])
         facts.widest_row_span = std::max(facts.widest_row_span, m.col_ind[m.row_ptr[row + 1] - 1] - m.col_ind[m.row_ptr[row]]);
-    if (layout == SPMV_LAYOUT_LP) facts.lane_packed_words[tpr_slot(tpr)] = lane_packed_word_count(m, tpr);
+    // CSR-lp of a large matrix is encoded on the device (encode.cu): the row_ptr and column arrays go up
+    // once and the layout (widths, row words, word count) comes from the GPU; smaller ones on the host
+    std::unique_ptr<spmv_operator> op(new spmv_operator);
+    const bool device_encode = layout == SPMV_LAYOUT_LP && m.nnz() >= kDeviceEncodeNnz;
+    DeviceBuffer<int> encode_columns;
+    if (device_encode) {
+      op->row_ptr = device_upload<int>(m.row_ptr.data(), (size_t)m.rows + 1, op->device_bytes);
+      encode_columns.allocate((size_t)m.nnz(), m.col_ind.data());
+      op->row_word = device_upload<int>(nullptr, (size_t)m.rows, op->device_bytes);
+      op->row_width = device_upload<uint8_t>(nullptr, (size_t)m.rows, op->device_bytes);
+      facts.lane_packed_words[tpr_slot(tpr)] =
+          device_lane_packed_layout(op->row_ptr, encode_columns.data, m.rows, tpr, op->row_word, op->row_width, nullptr);
+    } else if (layout == SPMV_LAYOUT_LP) {
+      facts.lane_packed_words[tpr_slot(tpr)] = lane_packed_word_count(m, tpr);
+    }
     if (!admissible(m, facts, layout, tpr))
       fail(SPMV_ERR_NOT_ADMISSIBLE, "layout not admissible for this matrix");
 
-    std::unique_ptr<spmv_operator> op(new spmv_operator);
     cuda_check(cudaGetDevice(&op->device), "cudaGetDevice");
     op->layout = layout;
     op->dtype = dtype;
@@ -336,7 +373,7 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
 
     // encoded streams
     const size_t nnz = (size_t)m.nnz();
-    op->row_ptr = device_upload<int>(m.row_ptr.data(), (size_t)m.rows + 1, op->device_bytes);
+    if (!op->row_ptr) op->row_ptr = device_upload<int>(m.row_ptr.data(), (size_t)m.rows + 1, op->device_bytes);
     {
       std::vector<unsigned char> converted(nnz * value_bytes);
       convert_values(dtype, m.val.data(), (int64_t)nnz, config->value_rounding, converted.data());
@@ -362,9 +399,19 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
       }
       default: {
         const int64_t word_count = facts.lane_packed_words[tpr_slot(tpr)];
-        std::vector<uint32_t> words((size_t)word_count);
         row_word.resize((size_t)m.rows);
         row_width.resize((size_t)m.rows);
+        if (device_encode) {
+          op->words = device_upload<uint32_t>(nullptr, (size_t)word_count, op->device_bytes);
+          device_lane_packed_pack(op->row_ptr, encode_columns.data, m.rows, tpr, op->row_word, op->row_width, op->words,
+                                  word_count, nullptr);
+          encode_columns.release();
+          cuda_check(cudaMemcpy(row_word.data(), op->row_word, sizeof(int) * row_word.size(), cudaMemcpyDeviceToHost),
+                     "row words");
+          cuda_check(cudaMemcpy(row_width.data(), op->row_width, row_width.size(), cudaMemcpyDeviceToHost), "row widths");
+          break;
+        }
+        std::vector<uint32_t> words((size_t)word_count);
         encode_lane_packed(m, tpr, word_count, row_word.data(), row_width.data(), words.data());
         op->words = device_upload<uint32_t>(words.data(), words.size(), op->device_bytes);
         op->row_word = device_upload<int>(row_word.data(), row_word.size(), op->device_bytes);

@@ -158,6 +158,7 @@ _sig("spmv_encode_row_base", _i, _v, _v)
 _sig("spmv_encode_relative", _i, _v, _i, _v)
 _sig("spmv_lane_packed_word_count", _i, _v, _i, ctypes.POINTER(_i64))
 _sig("spmv_encode_lane_packed", _i, _v, _i, _i64, _v, _v, _v)
+_sig("spmv_encode_lane_packed_device", _i, _v, _v, _i, _i, _v, _v, _v, _i64, ctypes.POINTER(_i64), _v)
 _sig("spmv_operator_config_init", None, ctypes.POINTER(OperatorConfig), _i, _i, _i)
 _sig("spmv_operator_create", _i, _v, ctypes.POINTER(OperatorConfig), _c_void_pp)
 _sig("spmv_operator_get_info", _i, _v, ctypes.POINTER(OperatorInfo))
@@ -435,6 +436,17 @@ def build_packed_deltas(matrix: CsrMatrix, tpr: int, word_count: Optional[int] =
     _check(_lib.spmv_encode_lane_packed(matrix.handle, tpr, word_count, _pointer(row_word), _pointer(row_width),
                                         _pointer(words)))
     return row_word[:rows], row_width[:rows], words
+
+
+def build_packed_deltas_device(row_ptr: int, col_ind: int, rows: int, tpr: int, row_word: int, row_width: int,
+                               words: int = 0, word_capacity: int = 0, stream: int = 0) -> int:
+    """build_packed_deltas on the GPU from device pointers (row_ptr int32[rows+1], col_ind int32[nnz]) into
+    device row_word int32[rows] and row_width uint8[rows], and words uint32 when given; returns the word
+    count (2 spare words included)."""
+    count = ctypes.c_int64()
+    _check(_lib.spmv_encode_lane_packed_device(row_ptr, col_ind, rows, tpr, row_word, row_width, words or None,
+                                               word_capacity, ctypes.byref(count), stream or None))
+    return count.value
 
 
 # ---------------------------------------------------------------------------------------------------
