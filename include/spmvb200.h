@@ -175,6 +175,18 @@ int spmv_encode_lane_packed(const spmv_csr* matrix, int tpr, int64_t word_count,
 int spmv_encode_lane_packed_device(const int* row_ptr, const int* col_ind, int rows, int tpr, int* row_word,
                                    uint8_t* row_width, uint32_t* words, int64_t word_capacity, int64_t* word_count,
                                    void* stream);
+/* The same encoding without allocating any device memory, for callers that must not allocate while they
+ * encode: a framework whose own caching allocator owns every device byte, code that reserves its memory up
+ * front under a fixed budget, loops that cannot stall on cudaMalloc/cudaFree. No counterpart in the
+ * reference (its encoder runs on the host). Limits: rows at most 2^26 (SPMV_ERR_TOO_LARGE above); the
+ * scratch is a fixed 512 KiB array inside the library, held on every GPU that loads it until the process
+ * exits. The first call on a device looks up that array's address on the device (make that first call
+ * before any stream capture). All calls share the array, so calls that overlap on the GPU (other streams,
+ * other host threads) race on it; nothing in it needs clearing between calls. Same arguments, results
+ * and two-call use as spmv_encode_lane_packed_device. */
+int spmv_encode_lane_packed_device_noalloc(const int* row_ptr, const int* col_ind, int rows, int tpr, int* row_word,
+                                           uint8_t* row_width, uint32_t* words, int64_t word_capacity,
+                                           int64_t* word_count, void* stream);
 
 /* ---- device operator: DeviceMatrix<T> + Configuration (bench_csr_width.cu:88, :128) ------------- */
 typedef struct spmv_operator spmv_operator;

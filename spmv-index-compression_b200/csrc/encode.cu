@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 
 #include "capi_internal.hpp"
@@ -201,6 +202,135 @@ extern "C" int spmv_encode_lane_packed_device(const int* row_ptr, const int* col
     require(word_capacity >= count, "words holds fewer than word_count words");
     device_lane_packed_pack(row_ptr, col_ind, rows, tpr, row_word, row_width, words, count, s);
     const cudaError_t status = cudaStreamSynchronize(s);
+    if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("CSR-lp packing on the device: ") + cudaGetErrorString(status));
+  });
+}
+
+// ---- the CSR-lp layout without allocating --------------------------------------------------------------
+// For callers that must not allocate device memory while they encode: a framework whose own caching
+// allocator owns every device byte (a cudaMalloc behind its back can fail or fragment its pool), code that
+// reserves all its memory up front under a fixed budget, and loops that cannot stall on cudaMalloc/cudaFree,
+// which may synchronise the device. The scan's scratch (one 64-bit sum per block of 1024 rows, and the
+// grand total) lives in this file-scope device array instead of a cudaMalloc'd buffer; the word count of
+// each row goes through the caller's own row_word.
+namespace spmvb200 {
+namespace {
+
+constexpr int64_t kNoAllocMaxBlocks = 65536;                          // rows up to 65536 * 1024 = 2^26
+static __device__ __align__(256) long long g_encode_scratch[kNoAllocMaxBlocks + 1];   // 512 KiB + 8 B
+
+// Widths, and each row's word count written to row_word (a row of fewer than 2^31 entries has fewer than
+// 2^31 words).
+__global__ void k_lp_widths_into(const int* __restrict__ row_ptr, const int* __restrict__ col, int rows, int tpr,
+                                 uint8_t* __restrict__ row_width, int* __restrict__ row_words) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) / 32;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; row < rows; row += warps) {
+    const int begin = row_ptr[row], end = row_ptr[row + 1];
+    unsigned widest = 0;
+    for (int entry = begin + lane; entry < end; entry += 32) {
+      const int delta = entry - begin < tpr ? col[entry] - col[begin] : col[entry] - col[entry - tpr];
+      widest = max(widest, (unsigned)delta);
+    }
+    widest = __reduce_max_sync(0xffffffffu, widest);
+    if (lane == 0) {
+      const int width = widest == 0 ? 0 : 32 - __clz((int)widest);
+      row_width[row] = (uint8_t)width;
+      row_words[row] = (int)(((long long)(end - begin) * width + 31) / 32);
+    }
+  }
+}
+
+// In place over row_word: the exclusive scan within each block of 1024 rows (64-bit sums, stored as int;
+// a block whose prefix does not fit makes a total above 2^31 words, which the caller rejects), and the
+// block's total into sums[block].
+__global__ void __launch_bounds__(kScanBlock) k_scan_blocks_in_place(int* __restrict__ row_word, int64_t count,
+                                                                   long long* __restrict__ sums) {
+  __shared__ long long warp_totals[kScanBlock / 32];
+  const int64_t index = (int64_t)blockIdx.x * kScanBlock + threadIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+  const long long value = index < count ? row_word[index] : 0;
+  long long inclusive = value;
+#pragma unroll
+  for (int offset = 1; offset < 32; offset <<= 1) {
+    const long long other = __shfl_up_sync(0xffffffffu, inclusive, offset);
+    if (lane >= offset) inclusive += other;
+  }
+  if (lane == 31) warp_totals[warp] = inclusive;
+  __syncthreads();
+  if (warp == 0) {
+    long long total = warp_totals[lane];
+#pragma unroll
+    for (int offset = 1; offset < 32; offset <<= 1) {
+      const long long other = __shfl_up_sync(0xffffffffu, total, offset);
+      if (lane >= offset) total += other;
+    }
+    warp_totals[lane] = total;
+  }
+  __syncthreads();
+  const long long before = warp == 0 ? 0 : warp_totals[warp - 1];
+  if (index < count) row_word[index] = (int)(before + inclusive - value);
+  if (threadIdx.x == kScanBlock - 1) sums[blockIdx.x] = before + inclusive;
+}
+
+__global__ void k_scan_add_in_place(const long long* __restrict__ sums, int64_t count, int* __restrict__ row_word) {
+  const int64_t index = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (index < count) row_word[index] = (int)(row_word[index] + sums[index / kScanBlock]);
+}
+
+// The address of g_encode_scratch on each device, taken once per device with that device current.
+long long* encode_scratch_address() {
+  static std::mutex guard;
+  static long long* address[64] = {};
+  int device = 0;
+  const cudaError_t status = cudaGetDevice(&device);
+  if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(status));
+  if (device < 0 || device >= 64) fail(SPMV_ERR_UNSUPPORTED, "device ordinal above 63");
+  std::lock_guard<std::mutex> lock(guard);
+  if (!address[device]) {
+    void* pointer = nullptr;
+    const cudaError_t found = cudaGetSymbolAddress(&pointer, g_encode_scratch);
+    if (found != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(found));
+    address[device] = static_cast<long long*>(pointer);
+  }
+  return address[device];
+}
+
+}  // namespace
+}  // namespace spmvb200
+
+extern "C" int spmv_encode_lane_packed_device_noalloc(const int* row_ptr, const int* col_ind, int rows, int tpr,
+                                                      int* row_word, uint8_t* row_width, uint32_t* words,
+                                                      int64_t word_capacity, int64_t* word_count, void* stream) {
+  return guarded([&] {
+    require(row_ptr && (col_ind || rows == 0) && row_word && row_width && word_count && rows >= 0, "bad arguments");
+    require(valid_tpr(tpr), "threads per row must be 2, 4, 8, 16 or 32");
+    const int64_t blocks = ((int64_t)rows + kScanBlock - 1) / kScanBlock;
+    if (blocks > kNoAllocMaxBlocks)
+      fail(SPMV_ERR_TOO_LARGE, "the allocation-free encoder takes at most " + std::to_string(kNoAllocMaxBlocks * kScanBlock) +
+                                   " rows (its fixed scratch holds one sum per 1024 rows); use spmv_encode_lane_packed_device");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    long long* scratch = encode_scratch_address();   // sums[0..blocks), then the total at [kNoAllocMaxBlocks]
+    long long total = 0;
+    cudaError_t status = cudaSuccess;
+    if (rows > 0) {
+      // every scratch entry this call reads is written by it first: nothing needs clearing
+      k_lp_widths_into<<<warp_blocks(rows), 256, 0, s>>>(row_ptr, col_ind, rows, tpr, row_width, row_word);
+      k_scan_blocks_in_place<<<(unsigned)blocks, kScanBlock, 0, s>>>(row_word, rows, scratch);
+      k_scan_sums<<<1, kScanBlock, 0, s>>>(scratch, blocks, scratch + kNoAllocMaxBlocks);
+      k_scan_add_in_place<<<(unsigned)(((int64_t)rows + 255) / 256), 256, 0, s>>>(scratch, rows, row_word);
+      status = cudaGetLastError();
+      if (status == cudaSuccess)
+        status = cudaMemcpyAsync(&total, scratch + kNoAllocMaxBlocks, sizeof(long long), cudaMemcpyDeviceToHost, s);
+      if (status == cudaSuccess) status = cudaStreamSynchronize(s);
+      if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("CSR-lp layout on the device: ") + cudaGetErrorString(status));
+    }
+    *word_count = total + 2;
+    if (total > INT32_MAX) fail(SPMV_ERR_NOT_ADMISSIBLE, "CSR-lp stream exceeds 2^31 words");
+    if (words == nullptr) return;
+    require(word_capacity >= total + 2, "words holds fewer than word_count words");
+    device_lane_packed_pack(row_ptr, col_ind, rows, tpr, row_word, row_width, words, total + 2, s);
+    status = cudaStreamSynchronize(s);
     if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("CSR-lp packing on the device: ") + cudaGetErrorString(status));
   });
 }

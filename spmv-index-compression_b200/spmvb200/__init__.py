@@ -159,6 +159,7 @@ _sig("spmv_encode_relative", _i, _v, _i, _v)
 _sig("spmv_lane_packed_word_count", _i, _v, _i, ctypes.POINTER(_i64))
 _sig("spmv_encode_lane_packed", _i, _v, _i, _i64, _v, _v, _v)
 _sig("spmv_encode_lane_packed_device", _i, _v, _v, _i, _i, _v, _v, _v, _i64, ctypes.POINTER(_i64), _v)
+_sig("spmv_encode_lane_packed_device_noalloc", _i, _v, _v, _i, _i, _v, _v, _v, _i64, ctypes.POINTER(_i64), _v)
 _sig("spmv_operator_config_init", None, ctypes.POINTER(OperatorConfig), _i, _i, _i)
 _sig("spmv_operator_create", _i, _v, ctypes.POINTER(OperatorConfig), _c_void_pp)
 _sig("spmv_operator_get_info", _i, _v, ctypes.POINTER(OperatorInfo))
@@ -446,6 +447,16 @@ def build_packed_deltas_device(row_ptr: int, col_ind: int, rows: int, tpr: int, 
     count = ctypes.c_int64()
     _check(_lib.spmv_encode_lane_packed_device(row_ptr, col_ind, rows, tpr, row_word, row_width, words or None,
                                                word_capacity, ctypes.byref(count), stream or None))
+    return count.value
+
+
+def build_packed_deltas_device_noalloc(row_ptr: int, col_ind: int, rows: int, tpr: int, row_word: int, row_width: int,
+                                       words: int = 0, word_capacity: int = 0, stream: int = 0) -> int:
+    """build_packed_deltas_device without allocating device memory (a fixed scratch array inside the
+    library; at most 2^26 rows; calls that overlap on the GPU race on that array)."""
+    count = ctypes.c_int64()
+    _check(_lib.spmv_encode_lane_packed_device_noalloc(row_ptr, col_ind, rows, tpr, row_word, row_width, words or None,
+                                                       word_capacity, ctypes.byref(count), stream or None))
     return count.value
 
 
