@@ -2,8 +2,9 @@
 // and chained products over nnz-balanced row shards with x replicated.
 //
 // A chained product y -> x: every rank multiplies its row shard into its slice of the next x, then the
-// slices are all-gathered. Shards differ in size after nnz balancing, so the all-gather is a group of
-// in-place broadcasts, one per rank (an all-gather of unequal pieces). NCCL is opened at run time
+// slices are all-gathered: one in-place ncclAllGather when the shards have equal rows, else (shards differ
+// in size after nnz balancing) a group of in-place broadcasts, one per rank (an all-gather of unequal
+// pieces). NCCL is opened at run time
 // (dlopen, reusing a libnccl.so.2 the process already loaded, e.g. PyTorch's), so the library does not
 // pin an NCCL version of its own.
 #include <cuda_runtime.h>
@@ -29,6 +30,7 @@ struct NcclApi {
   ncclResult_t (*group_start)() = nullptr;
   ncclResult_t (*group_end)() = nullptr;
   ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*get_error_string)(ncclResult_t) = nullptr;
   bool loaded = false;
 };
@@ -54,6 +56,7 @@ NcclApi& nccl() {
     bind(api.group_start, "ncclGroupStart");
     bind(api.group_end, "ncclGroupEnd");
     bind(api.broadcast, "ncclBroadcast");
+    bind(api.all_gather, "ncclAllGather");
     bind(api.get_error_string, "ncclGetErrorString");
     api.loaded = ok;
   });
@@ -170,18 +173,31 @@ int spmv_chain_run(const spmv_operator* shard_op, spmv_comm* comm, const int* sh
     NcclApi& api = nccl();
     char* current = static_cast<char*>(x_current);
     char* next = static_cast<char*>(x_next);
+    // shards of equal rows (and so slices of equal size) are gathered by one in-place all-gather; others by
+    // a group of broadcasts, one per rank (an all-gather of unequal pieces)
+    bool equal = true;
+    for (int root = 0; root < nranks; ++root)
+      equal = equal && shard_row_begin[root + 1] - shard_row_begin[root] == shard_row_begin[1] - shard_row_begin[0];
     for (int product = 0; product < products; ++product) {
       // this rank's rows of y go straight into its slice of the next x
       const int status = spmv_operator_run(shard_op, current, next + value_bytes * shard_row_begin[rank], stream);
       if (status != SPMV_OK) fail(status, spmv_last_error());
-      nccl_check(api.group_start(), "ncclGroupStart");
-      for (int root = 0; root < nranks; ++root) {
-        const size_t count = (size_t)(shard_row_begin[root + 1] - shard_row_begin[root]);
-        if (count == 0) continue;
-        char* slice = next + value_bytes * shard_row_begin[root];
-        nccl_check(api.broadcast(slice, slice, count, nccl_type(info.dtype), root, comm->comm, s), "ncclBroadcast");
+      if (equal) {
+        const size_t count = (size_t)(shard_row_begin[1] - shard_row_begin[0]);
+        if (count > 0)
+          nccl_check(api.all_gather(next + value_bytes * shard_row_begin[rank], next, count, nccl_type(info.dtype),
+                                    comm->comm, s),
+                     "ncclAllGather");
+      } else {
+        nccl_check(api.group_start(), "ncclGroupStart");
+        for (int root = 0; root < nranks; ++root) {
+          const size_t count = (size_t)(shard_row_begin[root + 1] - shard_row_begin[root]);
+          if (count == 0) continue;
+          char* slice = next + value_bytes * shard_row_begin[root];
+          nccl_check(api.broadcast(slice, slice, count, nccl_type(info.dtype), root, comm->comm, s), "ncclBroadcast");
+        }
+        nccl_check(api.group_end(), "ncclGroupEnd");
       }
-      nccl_check(api.group_end(), "ncclGroupEnd");
       std::swap(current, next);
     }
   });

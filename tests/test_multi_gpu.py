@@ -1,6 +1,7 @@
 """Chained products over NCCL on two GPUs (spmv_chain_run): each rank's CSR-lp shard product into its
-slice of the next x, the slices all-gathered, three times; the result bit-identical to the oracle's
-chain on the whole matrix."""
+slice of the next x, the slices all-gathered (grouped broadcasts for nnz-balanced shards of unequal rows,
+one all-gather for equal ones), three times; the result bit-identical to the oracle's chain on the whole
+matrix."""
 import datetime
 import os
 import socket
@@ -36,23 +37,24 @@ def worker(rank, world, port):
     dist.broadcast_object_list(box, src=0)
     comm = spmv.Comm(world, rank, box[0], device=rank)
     matrix = spmv.synth_random_band(20000, 500, 12.0, 3)
-    bounds = spmv.shard_rows(matrix, world)
-    shard = matrix.slice_rows(int(bounds[rank]), int(bounds[rank + 1]))
-    x0 = spmv.fill_uniform(spmv.F64, matrix.cols, 9)
-    with spmv.Operator(shard, spmv.LP, spmv.F64, 8, device=rank) as op:
-        x_current = torch.from_numpy(x0).cuda()
-        x_next = torch.zeros_like(x_current)
-        stream = torch.cuda.current_stream().cuda_stream
-        spmv.chain_run(op, comm, bounds, x_current.data_ptr(), x_next.data_ptr(), 3, stream)
-        comm.check(stream, 30000)
-        result = x_next.cpu().numpy()    # an odd count of products ends in x_next
     row_ptr, col_ind, values = matrix.arrays()
+    x0 = spmv.fill_uniform(spmv.F64, matrix.cols, 9)
     expected = x0.copy()
     for _ in range(3):
         expected = oracle.spmv_csr(row_ptr, col_ind, values, expected, spmv.F64, spmv.LP, 8)
+    # nnz-balanced shards (unequal: grouped broadcasts) and equal row halves (one all-gather)
+    for bounds in (spmv.shard_rows(matrix, world), np.array([0, 10000, 20000], dtype=np.int32)):
+        shard = matrix.slice_rows(int(bounds[rank]), int(bounds[rank + 1]))
+        with spmv.Operator(shard, spmv.LP, spmv.F64, 8, device=rank) as op:
+            x_current = torch.from_numpy(x0).cuda()
+            x_next = torch.zeros_like(x_current)
+            stream = torch.cuda.current_stream().cuda_stream
+            spmv.chain_run(op, comm, bounds, x_current.data_ptr(), x_next.data_ptr(), 3, stream)
+            comm.check(stream, 30000)
+            result = x_next.cpu().numpy()    # an odd count of products ends in x_next
+        assert np.array_equal(result.view(np.uint64), expected.view(np.uint64)), bounds.tolist()
     comm.close()
     dist.destroy_process_group()
-    assert np.array_equal(result.view(np.uint64), expected.view(np.uint64))
 
 
 def test_chained_products_over_nccl():
