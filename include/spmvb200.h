@@ -237,6 +237,7 @@ typedef struct {
   int schedule;              /* SPMV_SCHEDULE_TILES or SPMV_SCHEDULE_CLASSES                 */
   int64_t listed_rows;       /* classes: rows of more than 8 entries on groups of P threads  */
   int64_t blocks;            /* CTAs of one launch                                           */
+  int window_elements;       /* tiles: x elements a tile stages for its gathers (0: none)    */
 } spmv_operator_info;
 int spmv_operator_get_info(const spmv_operator* op, spmv_operator_info* info);
 

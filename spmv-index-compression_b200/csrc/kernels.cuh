@@ -30,6 +30,7 @@
 #pragma once
 
 #include <cuda_fp16.h>
+#include <climits>
 #include <cstdint>
 #include <type_traits>
 
@@ -96,6 +97,9 @@ struct KernelArgs {
   int tile_nnz;              // nonzeros a tile holds at most
   int tile_rows;             // rows a tile holds at most
   int tile_index_words;      // CSR-lp: stream words a tile's image holds at most
+  const int2* tile_windows;  // [tile_count] {first column, end column} of the x window a tile stages (first ==
+                             // end: none); null: no windows in this launch (x not 16-byte aligned)
+  int window_elements;       // x elements a tile's window holds at most
   int stages;                // shared-memory buffers of a tile CTA (1..kMaxStages)
   const int* row_list;       // rows of the vector path (nullptr: rows 0..row_count-1)
   int64_t row_count;         // entries of row_list, or rows
@@ -119,14 +123,16 @@ struct KernelArgs {
 // row_width slices and of its value and index (or CSR-lp word) ranges. An image starts at the 16-byte
 // boundary at or below its first element, so it holds up to 16 bytes before and after the range.
 struct StagePlan {
-  int header, row_ptr, row_base, row_word, row_width, values, index, bytes;
+  int header, row_ptr, row_base, row_word, row_width, values, index, window, bytes;
 };
 
 __host__ __device__ inline int round16(int bytes) { return (bytes + 15) & ~15; }
 
 // index_words: CSR-lp, the words a tile's stream image holds at most (the longest tile's word range plus
 // the word a delta may read past it); ignored by the other layouts, whose index image holds tile_nnz.
-__host__ __device__ inline StagePlan stage_plan(int tile_nnz, int tile_rows, int value_bytes, int layout, int index_words) {
+// window_elements: the x elements a tile's window of x holds at most (0: no window).
+__host__ __device__ inline StagePlan stage_plan(int tile_nnz, int tile_rows, int value_bytes, int layout, int index_words,
+                                                int window_elements) {
   const bool base = layout == SPMV_LAYOUT_R16 || layout == SPMV_LAYOUT_R8 || layout == SPMV_LAYOUT_LP;
   const bool packed = layout == SPMV_LAYOUT_LP;
   const int index_bytes = packed ? 4 : (layout == SPMV_LAYOUT_I32 ? 4 : ((layout == SPMV_LAYOUT_I16 || layout == SPMV_LAYOUT_R16) ? 2 : 1));
@@ -139,13 +145,14 @@ __host__ __device__ inline StagePlan stage_plan(int tile_nnz, int tile_rows, int
   plan.row_width = offset; if (packed) offset += round16(tile_rows) + 16;
   plan.values = offset;    offset += round16(value_bytes * tile_nnz) + 16;
   plan.index = offset;     offset += packed ? round16(4 * index_words) + 16 : round16(index_bytes * tile_nnz) + 16;
+  plan.window = offset;    if (window_elements > 0) offset += round16(value_bytes * window_elements) + 32;
   plan.bytes = offset;
   return plan;
 }
 
 __host__ __device__ inline int tile_smem_bytes(int tile_nnz, int tile_rows, int value_bytes, int layout, int stages,
-                                               int index_words) {
-  return 64 + stages * stage_plan(tile_nnz, tile_rows, value_bytes, layout, index_words).bytes;
+                                               int index_words, int window_elements) {
+  return 64 + stages * stage_plan(tile_nnz, tile_rows, value_bytes, layout, index_words, window_elements).bytes;
 }
 
 // ---- small device helpers -----------------------------------------------------------------------
@@ -388,6 +395,8 @@ struct TileView {
   const uint8_t* row_width_;
   const V* values_;
   const Index* index_;
+  const V* window_;   // x by absolute column, when the tile staged a window of x
+  bool windowed;
   __device__ __forceinline__ TileView(const unsigned char* stage, const StagePlan& plan) {
     const int* header = reinterpret_cast<const int*>(stage + plan.header);
     row_begin = header[0];
@@ -398,6 +407,13 @@ struct TileView {
     row_width_ = reinterpret_cast<const uint8_t*>(stage + plan.row_width) - header[4];
     values_ = reinterpret_cast<const V*>(stage + plan.values) - header[5];
     index_ = reinterpret_cast<const Index*>(stage + plan.index) - header[6];
+    if constexpr (LAYOUT != SPMV_LAYOUT_LP) {   // CSR-lp tiles never stage a window
+      windowed = header[7] != INT_MIN;
+      window_ = reinterpret_cast<const V*>(stage + plan.window) - (windowed ? header[7] : 0);
+    } else {
+      windowed = false;
+      window_ = nullptr;
+    }
   }
   __device__ __forceinline__ int row_ptr(int row) const { return row_ptr_[row]; }
   __device__ __forceinline__ int row_base(int row) const { return row_base_[row]; }
@@ -413,6 +429,8 @@ struct GlobalView {
   using Index = typename LayoutTraits<LAYOUT>::Index;
   const KernelArgs& a;
   uint64_t stream;
+  static constexpr bool windowed = false;
+  const V* window_ = nullptr;
   __device__ __forceinline__ explicit GlobalView(const KernelArgs& args) : a(args), stream(l2_stream_policy()) {}
   __device__ __forceinline__ int row_ptr(int row) const { return load_readonly(a.row_ptr + row); }
   __device__ __forceinline__ int row_base(int row) const { return load_readonly(a.row_base + row); }
@@ -555,7 +573,10 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
 #pragma unroll
             for (int j = 0; j < S; ++j) {
               const int e = entry + r * T + j * P;
-              if (e < entry_end) xv[r][j] = load_x(x + base + (int)tile.index(e), keep);
+              if (e < entry_end) {
+                const int column = base + (int)tile.index(e);
+                xv[r][j] = tile.windowed ? tile.window_[column] : load_x(x + column, keep);
+              }
             }
 #pragma unroll
           for (int r = 0; r < R; ++r)
@@ -609,6 +630,14 @@ __device__ __forceinline__ void issue_tile(const KernelArgs& a, int64_t tile_id,
   uint32_t bytes = row_ptr.bytes + values.bytes + index.bytes;
   if (kBase) bytes += row_base.bytes;
   if (kPacked) bytes += row_base.bytes + row_width.bytes;   // row_word has the extent of row_base
+  // the tile's window of x (columns [window.x, window.y)), when the plan gave it one: its gathers then read
+  // shared memory. x is 16-byte aligned whenever windows are on, and the plan keeps every window's 16-byte
+  // superset inside x.
+  const int2 window = !kPacked && a.tile_windows ? a.tile_windows[tile_id] : make_int2(0, 0);
+  const AlignedRange<V> x_window(static_cast<const V*>(a.x), window.x, window.y > window.x ? window.y : window.x);
+  const bool windowed = window.y > window.x;
+  header[7] = windowed ? (int)x_window.origin : INT_MIN;
+  if (windowed) bytes += x_window.bytes;
   mbarrier_arrive_expect_tx(full, bytes);
   // a range may be empty (a tile of empty rows has no values): no copy is issued for 0 bytes
   if (row_ptr.bytes)
@@ -625,6 +654,9 @@ __device__ __forceinline__ void issue_tile(const KernelArgs& a, int64_t tile_id,
     bulk_copy_g2s(smem_address(stage + plan.values), reinterpret_cast<const void*>(values.begin), values.bytes, full, stream);
   if (index.bytes)
     bulk_copy_g2s(smem_address(stage + plan.index), reinterpret_cast<const void*>(index.begin), index.bytes, full, stream);
+  if (windowed)
+    bulk_copy_g2s(smem_address(stage + plan.window), reinterpret_cast<const void*>(x_window.begin), x_window.bytes, full,
+                  l2_keep_policy());
 }
 
 // ---- rows longer than a tile ----------------------------------------------------------------------------
@@ -912,7 +944,7 @@ __global__ void __launch_bounds__(kTileBlock, 2) k_spmv_tiles(const KernelArgs a
   __shared__ int s_abort;
   __shared__ int s_released[kMaxStages];   // warps done with the buffer's current tile
   __shared__ int s_fills[kMaxStages];      // bulk fills issued into the buffer so far
-  const StagePlan plan = stage_plan(a.tile_nnz, a.tile_rows, (int)sizeof(V), LAYOUT, a.tile_index_words);
+  const StagePlan plan = stage_plan(a.tile_nnz, a.tile_rows, (int)sizeof(V), LAYOUT, a.tile_index_words, a.window_elements);
   const int stages = a.stages;
   const int64_t cta = (int64_t)blockIdx.x - a.vector_blocks;
   const int64_t ctas = (int64_t)gridDim.x - a.vector_blocks;

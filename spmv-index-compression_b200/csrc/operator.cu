@@ -14,6 +14,7 @@
 // The streams are the reference's (bench_csr_width.cu:795-951), so memory_of counts them exactly; the
 // tile plan adds 16 bytes per tile (about 2048 nonzeros) and 4 bytes per long row.
 #include <cuda_runtime.h>
+#include <climits>
 
 #include <cstring>
 #include <memory>
@@ -132,6 +133,54 @@ TilePlan plan_tiles(const Csr& matrix, int tile_nnz, int tile_rows, const int* r
   return plan;
 }
 
+// The x window of each tile: the columns [first column of its rows, last column of its rows] (rows are
+// sorted), kept when it holds at most limit elements and its 16-byte-aligned superset stays inside x
+// (cols elements of value_bytes, x 16-byte aligned); {0, 0} otherwise.
+std::vector<int2> plan_windows(const Csr& matrix, const TilePlan& plan, int limit, int value_bytes) {
+  std::vector<int2> windows(plan.tiles.size(), make_int2(0, 0));
+  const int64_t x_bytes = (int64_t)matrix.cols * value_bytes;
+  for (size_t t = 0; t < plan.tiles.size(); ++t) {
+    int first = INT32_MAX, last = -1;
+    for (int row = plan.tiles[t].x; row < plan.tiles[t].y; ++row) {
+      const int begin = matrix.row_ptr[row], end = matrix.row_ptr[row + 1];
+      if (end == begin) continue;
+      first = std::min(first, matrix.col_ind[begin]);
+      last = std::max(last, matrix.col_ind[end - 1]);
+    }
+    if (last < first) continue;
+    const int64_t end_bytes = ((int64_t)(last + 1) * value_bytes + 15) / 16 * 16;
+    if (last - first + 1 <= limit && end_bytes <= x_bytes) windows[t] = make_int2(first, last + 1);
+  }
+  return windows;
+}
+
+// Nonzeros per distinct 32-byte sector of x that a row reads, over the matrix: about 1 when the columns
+// of a row are scattered (every gather its own sector), several when they come in runs (stencils, blocks).
+double entries_per_x_sector(const Csr& matrix, int value_bytes) {
+  int64_t sectors = 0;
+  for (int row = 0; row < matrix.rows; ++row) {
+    int64_t previous = -1;
+    for (int entry = matrix.row_ptr[row]; entry < matrix.row_ptr[row + 1]; ++entry) {
+      const int64_t sector = (int64_t)matrix.col_ind[entry] * value_bytes / 32;
+      if (sector != previous) ++sectors;
+      previous = sector;
+    }
+  }
+  return sectors == 0 ? 0.0 : (double)matrix.nnz() / sectors;
+}
+
+// The window capacity worth reserving: the widest kept window when at least half the tiles keep one under
+// limit elements, else 0 (no windows).
+int window_capacity(const std::vector<int2>& windows) {
+  int kept = 0, widest = 0;
+  for (const int2& window : windows)
+    if (window.y > window.x) {
+      ++kept;
+      widest = std::max(widest, window.y - window.x);
+    }
+  return windows.empty() || 2 * kept < (int)windows.size() ? 0 : widest;
+}
+
 // Physical threads per row P: the fewest that leave a thread at most 28 entries of an average row (one
 // batch of gathers), and at least T/16 (at most 16 lane sums per thread; T/8 for CSR-lp, whose 16-lane
 // variants gather half as deep). A tile then holds 256/P rows (at least 128), so that one pass of the
@@ -223,6 +272,8 @@ struct spmv_operator {
   // rows by length (SPMV_SCHEDULE_CLASSES)
   int schedule = SPMV_SCHEDULE_TILES;
   int4* row_items = nullptr;
+  int2* tile_windows = nullptr;   // tiles: the x window each tile stages, {first, end} column (first == end: none)
+  int window_elements = 0;
   int64_t segment_first[6] = {0, 0, 0, 0, 0, 0};
   int64_t segment_items[6] = {0, 0, 0, 0, 0, 0};
   int64_t segment_blocks[6] = {0, 0, 0, 0, 0, 0};
@@ -234,7 +285,7 @@ struct spmv_operator {
     if (previous != device) cudaSetDevice(device);
     for (void* pointer : {(void*)row_ptr, values, columns, (void*)row_base, (void*)row_word, (void*)row_width,
                           (void*)words, (void*)tiles, (void*)tile_words, (void*)long_rows, (void*)status,
-                          (void*)row_items})
+                          (void*)row_items, (void*)tile_windows})
       if (pointer) cudaFree(pointer);
     if (previous >= 0 && previous != device) cudaSetDevice(previous);
   }
@@ -263,6 +314,9 @@ KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   a.tile_nnz = op->tile_nnz;
   a.tile_rows = op->tile_rows;
   a.tile_index_words = op->tile_index_words;
+  // x windows need x 16-byte aligned (the bulk copies of x start on 16-byte boundaries)
+  a.tile_windows = op->window_elements > 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 ? op->tile_windows : nullptr;
+  a.window_elements = op->window_elements;
   a.stages = op->stages;
   a.tile_ctas = op->tile_ctas;
   a.row_list = op->long_rows;
@@ -470,25 +524,46 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     auto plan_for = [&](int tile_nnz) {
       return plan_tiles(m, tile_nnz, op->tile_rows, packed ? row_word.data() : nullptr, packed ? row_width.data() : nullptr);
     };
-    auto smem_for = [&](int tile_nnz, const TilePlan* plan) {
-      return tile_smem_bytes(tile_nnz, op->tile_rows, value_bytes, layout, op->stages, plan ? plan->index_words : 0);
+    auto smem_for = [&](int tile_nnz, const TilePlan* plan, int window_elements) {
+      return tile_smem_bytes(tile_nnz, op->tile_rows, value_bytes, layout, op->stages, plan ? plan->index_words : 0,
+                             window_elements);
     };
     if (config->tile_nnz == 0 && !packed)
-      while (op->tile_nnz > 256 && smem_for(op->tile_nnz, nullptr) > budget) op->tile_nnz -= 256;
+      while (op->tile_nnz > 256 && smem_for(op->tile_nnz, nullptr, 0) > budget) op->tile_nnz -= 256;
     TilePlan plan = plan_for(op->tile_nnz);
     if (config->tile_nnz == 0 && packed)
-      while (op->tile_nnz > 256 && smem_for(op->tile_nnz, &plan) > budget) {
+      while (op->tile_nnz > 256 && smem_for(op->tile_nnz, &plan, 0) > budget) {
         op->tile_nnz -= 256;
         plan = plan_for(op->tile_nnz);
       }
+    // windows of x: when the gathers are scattered (under 1.5 nonzeros per x sector a row reads) and most
+    // tiles read x within at most 24 KB of columns (a random band), every tile stages that window with its
+    // streams and gathers from shared memory; the tiles then shrink to leave room for it. Not for CSR-lp,
+    // whose decode leaves no room (measured slower), nor where gathers come in runs (stencils: slower).
+    const int window_limit = 24 * 1024 / value_bytes;
+    std::vector<int2> windows;
+    if (!packed && entries_per_x_sector(m, value_bytes) < 1.5) {
+      windows = plan_windows(m, plan, window_limit, value_bytes);
+      op->window_elements = window_capacity(windows);
+    }
+    if (op->window_elements > 0) {
+      if (config->tile_nnz == 0)
+        while (op->tile_nnz > 256 && smem_for(op->tile_nnz, &plan, op->window_elements) > budget) {
+          op->tile_nnz -= 256;
+          plan = plan_for(op->tile_nnz);
+        }
+      windows = plan_windows(m, plan, op->window_elements, value_bytes);
+    }
     op->tile_index_words = plan.index_words;
-    const int smem = smem_for(op->tile_nnz, &plan);
+    const int smem = smem_for(op->tile_nnz, &plan, op->window_elements);
     if (smem > shared_limit)
       fail(SPMV_ERR_INVALID_ARGUMENT, "tiles need " + std::to_string(smem) + " bytes of shared memory, above the " +
                                           std::to_string(shared_limit) + " a block may have");
     op->tile_count = (int64_t)plan.tiles.size();
     op->long_count = (int64_t)plan.long_rows.size();
     op->tiles = device_upload<int4>(plan.tiles.data(), plan.tiles.size(), op->device_bytes);
+    if (op->window_elements > 0)
+      op->tile_windows = device_upload<int2>(windows.data(), windows.size(), op->device_bytes);
     if (layout == SPMV_LAYOUT_LP)
       op->tile_words = device_upload<int2>(plan.tile_words.data(), plan.tile_words.size(), op->device_bytes);
     op->long_rows = device_upload<int>(plan.long_rows.data(), plan.long_rows.size(), op->device_bytes);
@@ -532,6 +607,7 @@ int spmv_operator_get_info(const spmv_operator* op, spmv_operator_info* info) {
     info->listed_rows = 0;
     for (int segment = 0; segment < 6; ++segment) info->listed_rows += op->segment_items[segment];
     info->blocks = op->schedule == SPMV_SCHEDULE_CLASSES ? class_blocks(op) : op->long_ctas + op->tile_ctas;
+    info->window_elements = op->window_elements;
   });
 }
 

@@ -100,7 +100,8 @@ class OperatorInfo(ctypes.Structure):
                 ("tile_nnz", ctypes.c_int), ("tiles", ctypes.c_int64), ("tile_ctas", ctypes.c_int64),
                 ("stages", ctypes.c_int), ("tile_rows", ctypes.c_int), ("long_rows", ctypes.c_int64),
                 ("device_bytes", ctypes.c_int64), ("memory", MemoryBreakdown), ("schedule", ctypes.c_int),
-                ("listed_rows", ctypes.c_int64), ("blocks", ctypes.c_int64)]
+                ("listed_rows", ctypes.c_int64), ("blocks", ctypes.c_int64),
+                ("window_elements", ctypes.c_int)]
 
 
 class OperatorArrays(ctypes.Structure):

@@ -300,3 +300,23 @@ def test_large_lp_operator_encodes_on_the_device():
         with spmv.Operator(matrix, spmv.LP, spmv.F32, tpr) as op:
             y = device_run(op, x)
         assert np.array_equal(bits(y), bits(oracle_product(matrix, x, spmv.F32, spmv.LP, tpr))), tpr
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_x_windows_of_banded_tiles(dtype):
+    """A banded matrix: its tiles stage their window of x and gather from shared memory; every layout stays
+    bit-identical to the oracle, with x 16-byte aligned (windows on) and x offset by one element (windows off
+    for that launch)."""
+    matrix = spmv.synth_random_band(30000, 700, 20.0, 8)
+    x = spmv.fill_uniform(dtype, matrix.cols + 8, 4)
+    for layout, tpr in ((spmv.I32, 8), (spmv.R16, 32), (spmv.I16, 4), (spmv.I32, 2)):
+        with spmv.Operator(matrix, layout, dtype, tpr) as op:
+            assert op.info().window_elements > 0
+            x_device = torch.from_numpy(x).cuda()
+            for shift in (0, 2 if dtype == spmv.F16 else 1):
+                y_device = torch.full((op.rows,), float("nan"), dtype=TORCH[dtype], device="cuda")
+                op.run(x_device[shift:].data_ptr(), y_device.data_ptr(), 0)
+                torch.cuda.synchronize()
+                op.check()
+                expected = oracle_product(matrix, x[shift:shift + matrix.cols], dtype, layout, tpr)
+                assert np.array_equal(bits(y_device.cpu().numpy()), bits(expected)), (spmv.LAYOUT_NAMES[layout], tpr, shift)
