@@ -753,7 +753,25 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
         if (k >= 2) Read::sync(b);   // the gatherers are done with the columns of chunk k - 2
         int* columns = s_columns + b * chunk;
         if (lane < T) {
-          for (int i = lane; i < count; i += T, bit += width) {
+          // the words of every delta first (their positions do not depend on the decode), 8 at a time,
+          // then the running column
+          int i = lane;
+          for (; i + 7 * T < count; i += 8 * T) {
+            uint32_t delta[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint64_t at = bit + (uint64_t)k * width;
+              const uint64_t w = at >> 5;
+              delta[k] = __funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1), (uint32_t)(at & 31)) & mask;
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              column += (int)delta[k];
+              columns[i + k * T] = column;
+            }
+            bit += 8 * (uint64_t)width;
+          }
+          for (; i < count; i += T, bit += width) {
             const uint64_t w = bit >> 5;
             column += (int)(__funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1), (uint32_t)(bit & 31)) & mask);
             columns[i] = column;
