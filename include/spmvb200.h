@@ -248,6 +248,13 @@ int spmv_operator_run(const spmv_operator* op, const void* x, void* y, void* str
  * (result_at_fixed_tpr, bench_csr_width.cu:779). x_device and y_device are caller scratch on the device. */
 int spmv_operator_run_host(const spmv_operator* op, const void* x_host, void* y_host, void* x_device, void* y_device,
                            void* stream);
+/* A stream of products through host buffers: y_i = A x_i for i < count, x_i at x_host + i * x_stride bytes and
+ * y_i at y_host + i * y_stride (a stride of 0 reuses one buffer). The copy of x_{i+1} to the device, the
+ * product of x_i and the copy of y_{i-1} back overlap (the given stream and two internal ones); x_device and
+ * y_device are caller scratch for two vectors each, the second at an offset of the first's bytes rounded up
+ * to 16. Host buffers must be pinned for the copies to overlap. Returns when every y_i is on the host. */
+int spmv_operator_run_host_batch(const spmv_operator* op, const void* x_host, int64_t x_stride, void* y_host,
+                                 int64_t y_stride, int count, void* x_device, void* y_device, void* stream);
 /* Reads and clears the operator's device status word: SPMV_ERR_TIMEOUT if a bounded device-side wait
  * gave up since the last check. Synchronises the device. */
 int spmv_operator_check(const spmv_operator* op);

@@ -641,6 +641,56 @@ int spmv_operator_run_host(const spmv_operator* op, const void* x_host, void* y_
   });
 }
 
+int spmv_operator_run_host_batch(const spmv_operator* op, const void* x_host, int64_t x_stride, void* y_host,
+                                 int64_t y_stride, int count, void* x_device, void* y_device, void* stream) {
+  return guarded([&] {
+    require(op && x_host && y_host && x_device && y_device && count >= 0, "bad arguments");
+    const size_t value_bytes = (size_t)value_bytes_of(op->dtype);
+    const size_t x_bytes = value_bytes * (size_t)op->cols, y_bytes = value_bytes * (size_t)op->rows;
+    // device buffers b = 0, 1: x at x_device + b * x_bytes rounded up to 16 bytes, y likewise
+    const size_t x_pitch = (x_bytes + 15) / 16 * 16, y_pitch = (y_bytes + 15) / 16 * 16;
+    char* xd = static_cast<char*>(x_device);
+    char* yd = static_cast<char*>(y_device);
+    check_vector_alignment(op, xd, yd);
+    const cudaStream_t copy_in = static_cast<cudaStream_t>(stream);
+    cudaStream_t compute = nullptr, copy_out = nullptr;
+    cudaEvent_t copied_in[2] = {}, computed[2] = {}, copied_out[2] = {};
+    cudaError_t status = cudaStreamCreateWithFlags(&compute, cudaStreamNonBlocking);
+    if (status == cudaSuccess) status = cudaStreamCreateWithFlags(&copy_out, cudaStreamNonBlocking);
+    for (int b = 0; b < 2 && status == cudaSuccess; ++b) {
+      status = cudaEventCreateWithFlags(&copied_in[b], cudaEventDisableTiming);
+      if (status == cudaSuccess) status = cudaEventCreateWithFlags(&computed[b], cudaEventDisableTiming);
+      if (status == cudaSuccess) status = cudaEventCreateWithFlags(&copied_out[b], cudaEventDisableTiming);
+    }
+    // vector i uses buffers i mod 2: its copy in waits until the product of vector i - 2 has read x, its
+    // product until the copy out of vector i - 2 has read y; the three streams overlap the rest
+    for (int i = 0; i < count && status == cudaSuccess; ++i) {
+      const int b = i & 1;
+      const char* xh = static_cast<const char*>(x_host) + (int64_t)i * x_stride;
+      char* yh = static_cast<char*>(y_host) + (int64_t)i * y_stride;
+      if (i >= 2) status = cudaStreamWaitEvent(copy_in, computed[b], 0);
+      if (status == cudaSuccess) status = cudaMemcpyAsync(xd + b * x_pitch, xh, x_bytes, cudaMemcpyHostToDevice, copy_in);
+      if (status == cudaSuccess) status = cudaEventRecord(copied_in[b], copy_in);
+      if (status == cudaSuccess) status = cudaStreamWaitEvent(compute, copied_in[b], 0);
+      if (status == cudaSuccess && i >= 2) status = cudaStreamWaitEvent(compute, copied_out[b], 0);
+      if (status == cudaSuccess) status = launch_product(op, kernel_args(op, xd + b * x_pitch, yd + b * y_pitch), compute);
+      if (status == cudaSuccess) status = cudaEventRecord(computed[b], compute);
+      if (status == cudaSuccess) status = cudaStreamWaitEvent(copy_out, computed[b], 0);
+      if (status == cudaSuccess) status = cudaMemcpyAsync(yh, yd + b * y_pitch, y_bytes, cudaMemcpyDeviceToHost, copy_out);
+      if (status == cudaSuccess) status = cudaEventRecord(copied_out[b], copy_out);
+    }
+    if (status == cudaSuccess && count > 0) status = cudaStreamWaitEvent(copy_in, copied_out[(count - 1) & 1], 0);
+    if (status == cudaSuccess) status = cudaStreamSynchronize(copy_in);
+    if (status == cudaSuccess) status = cudaStreamSynchronize(copy_out);
+    for (int b = 0; b < 2; ++b)
+      for (cudaEvent_t event : {copied_in[b], computed[b], copied_out[b]})
+        if (event) cudaEventDestroy(event);
+    if (compute) cudaStreamDestroy(compute);
+    if (copy_out) cudaStreamDestroy(copy_out);
+    cuda_check(status, "batched product through host buffers");
+  });
+}
+
 int spmv_operator_check(const spmv_operator* op) {
   int timed_out = 0;
   const int status = guarded([&] {

@@ -166,6 +166,7 @@ _sig("spmv_operator_create", _i, _v, ctypes.POINTER(OperatorConfig), _c_void_pp)
 _sig("spmv_operator_get_info", _i, _v, ctypes.POINTER(OperatorInfo))
 _sig("spmv_operator_run", _i, _v, _v, _v, _v)
 _sig("spmv_operator_run_host", _i, _v, _v, _v, _v, _v, _v)
+_sig("spmv_operator_run_host_batch", _i, _v, _v, _i64, _v, _i64, _i, _v, _v, _v)
 _sig("spmv_operator_check", _i, _v)
 _sig("spmv_operator_get_arrays", _i, _v, ctypes.POINTER(OperatorArrays))
 _sig("spmv_operator_destroy", None, _v)
@@ -580,6 +581,14 @@ class Operator:
         host = lambda array: array if isinstance(array, int) else _pointer(array)  # noqa: E731
         _check(_lib.spmv_operator_run_host(self._handle, host(x_host), host(y_host), x_device, y_device,
                                            stream or None))
+
+    def run_host_batch(self, x_host, x_stride: int, y_host, y_stride: int, count: int, x_device: int, y_device: int,
+                       stream: int = 0):
+        """count products through host buffers with the copies in, the products and the copies out overlapped;
+        x_device / y_device hold two vectors each (the second 16-byte aligned after the first)."""
+        host = lambda array: array if isinstance(array, int) else _pointer(array)  # noqa: E731
+        _check(_lib.spmv_operator_run_host_batch(self._handle, host(x_host), x_stride, host(y_host), y_stride, count,
+                                                 x_device, y_device, stream or None))
 
     def check(self):
         """Raises SpmvError(ERR_TIMEOUT) if a bounded device-side wait gave up since the last check."""

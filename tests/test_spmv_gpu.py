@@ -320,3 +320,21 @@ def test_x_windows_of_banded_tiles(dtype):
                 op.check()
                 expected = oracle_product(matrix, x[shift:shift + matrix.cols], dtype, layout, tpr)
                 assert np.array_equal(bits(y_device.cpu().numpy()), bits(expected)), (spmv.LAYOUT_NAMES[layout], tpr, shift)
+
+
+def test_run_host_batch_pipelines_a_stream_of_vectors(ragged):
+    """Five different x vectors through host buffers with overlapped copies: every y as run() gives it."""
+    dtype = spmv.F64
+    count = 5
+    xs = np.stack([spmv.fill_uniform(dtype, ragged.cols, 20 + i) for i in range(count)])
+    ys = np.full((count, ragged.rows), np.nan)
+    x_pinned = torch.from_numpy(xs).pin_memory()
+    y_pinned = torch.from_numpy(ys).pin_memory()
+    pitch = lambda n: (n * 8 + 15) // 16 * 16 // 8  # noqa: E731
+    x_device = torch.empty(2 * pitch(ragged.cols), dtype=torch.float64, device="cuda")
+    y_device = torch.empty(2 * pitch(ragged.rows), dtype=torch.float64, device="cuda")
+    with spmv.Operator(ragged, spmv.LP, dtype, 8) as op:
+        op.run_host_batch(x_pinned.data_ptr(), ragged.cols * 8, y_pinned.data_ptr(), ragged.rows * 8, count,
+                          x_device.data_ptr(), y_device.data_ptr())
+        for i in range(count):
+            assert np.array_equal(bits(y_pinned[i].numpy()), bits(device_run(op, xs[i]))), i
