@@ -338,3 +338,17 @@ def test_run_host_batch_pipelines_a_stream_of_vectors(ragged):
                           x_device.data_ptr(), y_device.data_ptr())
         for i in range(count):
             assert np.array_equal(bits(y_pinned[i].numpy()), bits(device_run(op, xs[i]))), i
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_block_rows_of_column_runs(dtype):
+    """8x8-block rows (64 nonzeros in runs of 8 columns): 8 threads a row, two 32-row passes a tile; every
+    layout bit-identical to the oracle."""
+    matrix = spmv.synth_block_fem(20000, 8, 8, 2000, 4, 0, 20000)
+    x = spmv.fill_uniform(dtype, matrix.cols, 6)
+    for layout, tpr in ((spmv.I32, 8), (spmv.R16, 16), (spmv.I16, 32), (spmv.LP, 8)):
+        with spmv.Operator(matrix, layout, dtype, tpr) as op:
+            if layout != spmv.LP:
+                assert op.info().physical_tpr == 8 and op.info().tile_rows == 64
+            y = device_run(op, x)
+        assert np.array_equal(bits(y), bits(oracle_product(matrix, x, dtype, layout, tpr))), (spmv.LAYOUT_NAMES[layout], tpr)
