@@ -58,6 +58,9 @@ def parse_args():
     parser.add_argument("--tpr", type=int, default=8)
     parser.add_argument("--physical-tpr", type=int, default=0)
     parser.add_argument("--tile-nnz", type=int, default=0)
+    parser.add_argument("--blocks-per-rank", type=int, default=0,
+                        help="fem: interleaved row blocks per rank whose all-gathers overlap the next block's "
+                             "product (0: 4 on more than one GPU, else 1; 1: one shard and spmv_chain_run)")
     parser.add_argument("--no-sweep", action="store_true", help="skip the per-layout/T table and comparators")
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget")
     return parser.parse_args()
@@ -392,9 +395,12 @@ def run_ours(args, rank, world, local_rank):
 
 
 def run_fem(args, rank, world, local_rank):
-    """Config 5: the block-FEM matrix row-sharded over the ranks (each rank builds only its rows), a step is
-    one chained product: every rank's shard product into its slice of the next x, then the slices
-    all-gathered over NCCL (spmv_chain_run). The kernel alone is also timed for the roofline."""
+    """The block-FEM matrix row-sharded over the ranks (each rank builds only its rows), a step is one
+    chained product. On one shard per rank (spmv_chain_run): every rank's shard product into its slice of
+    the next x, then the slices all-gathered over NCCL. On interleaved row blocks (spmv_chain_run_blocks,
+    the default on more than one GPU): rank r holds blocks c * world + r of 32M / (world * C) rows, and each
+    round of blocks is all-gathered while the next block computes. The kernel alone is also timed for the
+    roofline."""
     import torch
     import spmvb200 as spmv
     dist = None
@@ -405,17 +411,27 @@ def run_fem(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(device)
     dtype_code = spmv.DTYPE_BY_NAME["fp32"]
     layout = spmv.LAYOUT_BY_NAME[args.layout]
-    bounds = fem_bounds(world)
-    shard = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, int(bounds[rank]), int(bounds[rank + 1]))
+    blocks_per_rank = args.blocks_per_rank or (4 if world > 1 else 1)
     total_nnz = 64 * FEM_ROWS
-    facts = spmv.facts_of(shard)
-    if not spmv.configuration_admissible(shard, facts, spmv.Configuration.of(layout, dtype_code, args.tpr)):
-        raise SystemExit(f"layout {args.layout} at T={args.tpr} is not admissible for fem")
-    op = spmv.Operator(shard, layout, dtype_code, args.tpr, physical_tpr=args.physical_tpr, tile_nnz=args.tile_nnz,
-                       device=local_rank)
-    info = op.info()
-    algorithmic_bytes = info.memory.total
-    del shard
+    if blocks_per_rank == 1:
+        bounds = fem_bounds(world)
+        ranges = [(int(bounds[rank]), int(bounds[rank + 1]))]
+    else:
+        block_rows = FEM_ROWS // (world * blocks_per_rank)
+        if block_rows * world * blocks_per_rank != FEM_ROWS or block_rows % 8:
+            raise SystemExit(f"{FEM_ROWS} rows do not divide into {world * blocks_per_rank} blocks of whole 8x8 blocks")
+        ranges = [((c * world + rank) * block_rows, (c * world + rank + 1) * block_rows) for c in range(blocks_per_rank)]
+    ops = []
+    for first, last in ranges:
+        shard = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, first, last)
+        facts = spmv.facts_of(shard)
+        if not spmv.configuration_admissible(shard, facts, spmv.Configuration.of(layout, dtype_code, args.tpr)):
+            raise SystemExit(f"layout {args.layout} at T={args.tpr} is not admissible for fem")
+        ops.append(spmv.Operator(shard, layout, dtype_code, args.tpr, physical_tpr=args.physical_tpr,
+                                 tile_nnz=args.tile_nnz, device=local_rank))
+        del shard
+    info = ops[0].info()
+    algorithmic_bytes = sum(op.info().memory.total for op in ops)
     box = [spmv.comm_unique_id() if rank == 0 else None]
     if dist is not None:
         dist.broadcast_object_list(box, src=0)
@@ -423,15 +439,19 @@ def run_fem(args, rank, world, local_rank):
     x_host = spmv.fill_uniform(dtype_code, FEM_ROWS, SEED_OF["fem"])
     x_current = torch.from_numpy(x_host).to(device)
     x_next = torch.zeros_like(x_current)
-    y_alone = torch.empty(int(bounds[rank + 1] - bounds[rank]), dtype=torch.float32, device=device)
+    y_alone = torch.empty(max(last - first for first, last in ranges), dtype=torch.float32, device=device)
 
     def barrier():
         if dist is not None:
             dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize()
 
-    chain = lambda count: spmv.chain_run(op, comm, bounds, x_current.data_ptr(), x_next.data_ptr(), count,  # noqa: E731
-                                         stream.cuda_stream)
+    if blocks_per_rank == 1:
+        chain = lambda count: spmv.chain_run(ops[0], comm, bounds, x_current.data_ptr(), x_next.data_ptr(),  # noqa: E731
+                                             count, stream.cuda_stream)
+    else:
+        chain = lambda count: spmv.chain_run_blocks(ops, block_rows, comm, x_current.data_ptr(),  # noqa: E731
+                                                    x_next.data_ptr(), count, stream.cuda_stream)
     chain(args.warmup)
     comm.check(stream.cuda_stream, 120000)
     barrier()
@@ -448,21 +468,28 @@ def run_fem(args, rank, world, local_rank):
     barrier()
     clocks = sampler.stop()
     elapsed_ms = start.elapsed_time(end)
-    # the product kernel alone on this rank's shard (x held still), for the roofline
-    kernel_ms = event_ms(torch, stream, lambda: op.run(x_current.data_ptr(), y_alone.data_ptr(), stream.cuda_stream),
-                         max(3, min(args.steps, 50)))
+
+    # the product kernels alone on this rank's rows (x held still), for the roofline
+    def products_alone():
+        for op in ops:
+            op.run(x_current.data_ptr(), y_alone.data_ptr(), stream.cuda_stream)
     kernel_steps = max(3, min(args.steps, 50))
-    op.check()
-    # end to end: x in from pinned host memory, one chained product, this rank's new slice of x out
+    kernel_ms = event_ms(torch, stream, products_alone, kernel_steps)
+    for op in ops:
+        op.check()
+    # end to end: x in from pinned host memory, one chained product, this rank's new rows of x out
     x_pinned = torch.from_numpy(x_host).pin_memory()
-    slice_rows = int(bounds[rank + 1] - bounds[rank])
-    y_pinned = torch.empty(slice_rows, dtype=torch.float32).pin_memory()
+    own_rows = sum(last - first for first, last in ranges)
+    y_pinned = torch.empty(own_rows, dtype=torch.float32).pin_memory()
     e2e_steps = max(1, min(args.steps, 10))
 
     def e2e_step():
         x_current.copy_(x_pinned, non_blocking=True)
         chain(1)
-        y_pinned.copy_(x_next[int(bounds[rank]):int(bounds[rank + 1])], non_blocking=True)
+        offset = 0
+        for first, last in ranges:
+            y_pinned[offset:offset + last - first].copy_(x_next[first:last], non_blocking=True)
+            offset += last - first
     barrier()
     e2e_ms = event_ms(torch, stream, e2e_step, e2e_steps)
     comm.check(stream.cuda_stream, 120000)
@@ -478,24 +505,32 @@ def run_fem(args, rank, world, local_rank):
     kernel_ms_per_launch = kernel_ms / kernel_steps
     achieved_gbs = algorithmic_bytes / (kernel_ms_per_launch * 1e-3) / 1e9
     peak, peak_source = measured_peak()
+    if blocks_per_rank == 1:
+        parallelism = (f"row shards x{world} (block-aligned, nnz-balanced), NCCL all-gather of y between chained "
+                       "products")
+    else:
+        parallelism = (f"interleaved row blocks x{world * blocks_per_rank} ({blocks_per_rank} per rank, "
+                       f"{block_rows} rows each), each round's NCCL all-gather beside the next block's product")
     line = {
         "metric": METRIC, "value": round(2.0 * total_nnz * args.steps / (elapsed_ms * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": WORKLOADS["fem"], "layout": args.layout, "tpr": args.tpr, "rows": FEM_ROWS,
-                   "nnz": total_nnz, "parallelism": f"row shards x{world} (block-aligned, nnz-balanced), NCCL all-gather "
-                                                   "of y between chained products",
+                   "nnz": total_nnz, "parallelism": parallelism,
                    "l2": f"no flush: {algorithmic_bytes / 1e9:.2f} GB per rank > 126 MB L2",
-                   "physical_tpr": info.physical_tpr, "tile_nnz": info.tile_nnz, "tiles": info.tiles},
+                   "physical_tpr": info.physical_tpr, "tile_nnz": info.tile_nnz,
+                   "tiles": sum(op.info().tiles for op in ops)},
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved_gbs / peak, 4), "traffic": None, "peak_source": peak_source,
-                     "kernel": "k_spmv_tiles", "algorithmic_bytes_per_launch": algorithmic_bytes,
-                     "kernel_ms": round(kernel_ms_per_launch, 6)},
+                     "kernel": "k_spmv_tiles", "algorithmic_bytes_per_launch": algorithmic_bytes // len(ops),
+                     "kernel_ms": round(kernel_ms_per_launch / len(ops), 6)},
         "clocks": clocks,
         "e2e": {"value": round(2.0 * total_nnz * e2e_steps / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
                 "h2d_bytes_per_step": FEM_ROWS * 4 * world, "d2h_bytes_per_step": FEM_ROWS * 4, "steps": e2e_steps},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * len(ops),
     }
+    for op in ops:
+        op.close()
     print(json.dumps(line), flush=True)
 
 

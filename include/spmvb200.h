@@ -349,6 +349,18 @@ int spmv_comm_check(spmv_comm* comm, void* stream, int timeout_ms);
 int spmv_chain_run(const spmv_operator* shard_op, spmv_comm* comm, const int* shard_row_begin, void* x_current,
                    void* x_next, int products, void* stream);
 
+/* Chained products over interleaved row blocks, each block round's all-gather beside the next block's
+ * product. The square matrix's n = nranks * blocks_per_rank * block_rows rows are cut into blocks of
+ * block_rows; rank r holds block_ops[c] for block c * nranks + r (c = 0 .. blocks_per_rank-1), each an
+ * operator of block_rows rows and n columns. Every product runs the rank's blocks in order into their
+ * places in the next x; the round of blocks c * nranks .. c * nranks + nranks - 1 is all-gathered in
+ * place on a stream of the communicator's own while block c + 1 computes, and the products leave a few
+ * multiprocessors to those collectives. Results are those of spmv_chain_run; x_current, x_next, the
+ * parity of products and the stream mean the same. No counterpart in the reference (its benchmark is
+ * single-GPU). */
+int spmv_chain_run_blocks(const spmv_operator* const* block_ops, int blocks_per_rank, int block_rows,
+                          spmv_comm* comm, void* x_current, void* x_next, int products, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

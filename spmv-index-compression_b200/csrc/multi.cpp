@@ -15,6 +15,7 @@
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <vector>
 
 #include "capi_internal.hpp"
 
@@ -86,7 +87,12 @@ struct spmv_comm {
   int rank = 0;
   int device = 0;
   bool aborted = false;
+  cudaStream_t side = nullptr;   // the all-gathers of spmv_chain_run_blocks, beside the products
 };
+
+namespace spmvb200 {
+cudaError_t run_operator_leaving_sms(const spmv_operator* op, const void* x, void* y, cudaStream_t stream, int free_sms);
+}
 
 using namespace spmvb200;
 
@@ -123,6 +129,7 @@ int spmv_comm_create(int nranks, int rank, const void* id128, int device, spmv_c
 
 void spmv_comm_destroy(spmv_comm* comm) {
   if (!comm) return;
+  if (comm->side) cudaStreamDestroy(comm->side);
   if (comm->comm) {
     if (comm->aborted) nccl().comm_abort(comm->comm);
     else nccl().comm_destroy(comm->comm);
@@ -200,6 +207,73 @@ int spmv_chain_run(const spmv_operator* shard_op, spmv_comm* comm, const int* sh
       }
       std::swap(current, next);
     }
+  });
+}
+
+// Multiprocessors the products leave to the all-gathers running beside them.
+constexpr int kCollectiveSms = 8;
+
+int spmv_chain_run_blocks(const spmv_operator* const* block_ops, int blocks_per_rank, int block_rows, spmv_comm* comm,
+                          void* x_current, void* x_next, int products, void* stream) {
+  return guarded([&] {
+    require(block_ops && blocks_per_rank >= 1 && block_rows >= 1 && comm && comm->comm && x_current && x_next &&
+                products >= 0,
+            "bad arguments");
+    require(!comm->aborted, "the communicator was aborted");
+    const int nranks = comm->nranks, rank = comm->rank;
+    const int64_t n = (int64_t)nranks * blocks_per_rank * block_rows;
+    spmv_operator_info info;
+    for (int c = 0; c < blocks_per_rank; ++c) {
+      if (!block_ops[c] || spmv_operator_get_info(block_ops[c], &info) != SPMV_OK) fail(SPMV_ERR_INVALID_ARGUMENT, "bad operator");
+      require(info.rows == block_rows && info.cols == n, "every block operator must have block_rows rows and n columns");
+    }
+    const int dtype = info.dtype;
+    const size_t value_bytes = (size_t)value_bytes_of(dtype);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    NcclApi& api = nccl();
+    if (!comm->side) {
+      const cudaError_t created = cudaStreamCreateWithFlags(&comm->side, cudaStreamNonBlocking);
+      if (created != cudaSuccess) {
+        comm->side = nullptr;
+        fail(SPMV_ERR_CUDA, std::string("cudaStreamCreateWithFlags: ") + cudaGetErrorString(created));
+      }
+    }
+    // computed[c]: block c's product of the current x is in place; computed[blocks_per_rank]: the last round
+    // of all-gathers is done
+    struct Events {
+      std::vector<cudaEvent_t> e;
+      ~Events() {
+        for (cudaEvent_t event : e)
+          if (event) cudaEventDestroy(event);
+      }
+    } events;
+    events.e.assign((size_t)blocks_per_rank + 1, nullptr);
+    std::vector<cudaEvent_t>& computed = events.e;
+    cudaEvent_t& gathered = events.e[(size_t)blocks_per_rank];
+    cudaError_t status = cudaSuccess;
+    for (cudaEvent_t& event : events.e)
+      if (status == cudaSuccess) status = cudaEventCreateWithFlags(&event, cudaEventDisableTiming);
+    char* current = static_cast<char*>(x_current);
+    char* next = static_cast<char*>(x_next);
+    for (int product = 0; product < products && status == cudaSuccess; ++product) {
+      for (int c = 0; c < blocks_per_rank && status == cudaSuccess; ++c) {
+        // block c * nranks + rank of y into its place in the next x; then, beside the next block's product,
+        // the round of blocks c * nranks .. c * nranks + nranks - 1 all-gathered in place
+        const int64_t mine = ((int64_t)c * nranks + rank) * block_rows;
+        status = run_operator_leaving_sms(block_ops[c], current, next + value_bytes * mine, s, kCollectiveSms);
+        if (status == cudaSuccess) status = cudaEventRecord(computed[c], s);
+        if (status == cudaSuccess) status = cudaStreamWaitEvent(comm->side, computed[c], 0);
+        if (status != cudaSuccess) break;
+        nccl_check(api.all_gather(next + value_bytes * mine, next + value_bytes * (int64_t)c * nranks * block_rows,
+                                  (size_t)block_rows, nccl_type(dtype), comm->comm, comm->side),
+                   "ncclAllGather");
+      }
+      // the next product reads this one's x: it waits for every round of the all-gather
+      if (status == cudaSuccess) status = cudaEventRecord(gathered, comm->side);
+      if (status == cudaSuccess) status = cudaStreamWaitEvent(s, gathered, 0);
+      std::swap(current, next);
+    }
+    if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("chained products over row blocks: ") + cudaGetErrorString(status));
   });
 }
 

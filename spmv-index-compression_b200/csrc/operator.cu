@@ -274,6 +274,7 @@ struct spmv_operator {
   int4* row_items = nullptr;
   int2* tile_windows = nullptr;   // tiles: the x window each tile stages, {first, end} column (first == end: none)
   int window_elements = 0;
+  int resident = 1;   // tiles: persistent CTAs per multiprocessor
   int64_t segment_first[6] = {0, 0, 0, 0, 0, 0};
   int64_t segment_items[6] = {0, 0, 0, 0, 0, 0};
   int64_t segment_blocks[6] = {0, 0, 0, 0, 0, 0};
@@ -348,6 +349,18 @@ cudaError_t launch_product(const spmv_operator* op, const KernelArgs& a, cudaStr
 }
 
 }  // namespace
+
+namespace spmvb200 {
+// One product on a stream, the tile kernel's persistent CTAs leaving free_sms multiprocessors idle, so that
+// kernels on other streams (a collective) run beside it. The class schedule needs no reservation: its
+// CTAs are not persistent.
+cudaError_t run_operator_leaving_sms(const spmv_operator* op, const void* x, void* y, cudaStream_t stream, int free_sms) {
+  KernelArgs a = kernel_args(op, x, y);
+  if (op->schedule == SPMV_SCHEDULE_TILES && free_sms > 0 && a.tile_ctas > 0)
+    a.tile_ctas = std::max<int64_t>(1, std::min<int64_t>(a.tile_ctas, a.tile_ctas - (int64_t)free_sms * op->resident));
+  return launch_product(op, a, stream);
+}
+}  // namespace spmvb200
 
 extern "C" {
 
@@ -586,6 +599,7 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     const int resident = tiles_occupancy(dtype, layout, tpr, op->physical_tpr, op->smem_bytes);
     if (resident <= 0 && (op->tile_count > 0 || op->long_count > 0))
       fail(SPMV_ERR_CUDA, "tile kernel cannot be resident with this configuration");
+    op->resident = std::max(1, resident);
     op->tile_ctas = std::min<int64_t>(op->tile_count, (int64_t)std::max(1, resident) * multiprocessors);
     op->long_ctas = std::min<int64_t>(op->long_count, (int64_t)std::max(1, resident) * multiprocessors);
     if (op->tile_ctas + op->long_ctas > 0x7fffffff) fail(SPMV_ERR_TOO_LARGE, "grid exceeds 2^31-1 blocks");

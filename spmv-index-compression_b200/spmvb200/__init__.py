@@ -186,6 +186,7 @@ _sig("spmv_comm_create", _i, _i, _i, _v, _i, _c_void_pp)
 _sig("spmv_comm_destroy", None, _v)
 _sig("spmv_comm_check", _i, _v, _v, _i)
 _sig("spmv_chain_run", _i, _v, _v, _v, _v, _v, _i, _v)
+_sig("spmv_chain_run_blocks", _i, _v, _i, _i, _v, _v, _v, _i, _v)
 
 
 def _check(status: int):
@@ -659,6 +660,35 @@ def chain_run(shard_op: "Operator", comm: Comm, shard_row_begin, x_current: int,
     bounds = np.ascontiguousarray(shard_row_begin, dtype=np.int32)
     _check(_lib.spmv_chain_run(shard_op.handle, comm.handle, _pointer(bounds), x_current, x_next, products,
                                stream or None))
+
+
+def chain_run_blocks(block_ops: Sequence["Operator"], block_rows: int, comm: Comm, x_current: int, x_next: int,
+                     products: int, stream: int = 0):
+    """products chained y -> x over interleaved row blocks: block_ops[c] holds rows of block
+    c * nranks + rank (block_rows rows, all n columns); each round's all-gather runs beside the next
+    block's product. Results, and where they are left, as chain_run's."""
+    handles = (ctypes.c_void_p * len(block_ops))(*[op.handle.value for op in block_ops])
+    _check(_lib.spmv_chain_run_blocks(handles, len(block_ops), block_rows, comm.handle, x_current, x_next, products,
+                                      stream or None))
+
+
+def interleaved_block_rows(row_ptr, col_ind, values, nranks: int, blocks_per_rank: int, rank: int):
+    """The CSR arrays (row_ptr, col_ind, values) of each of rank's interleaved row blocks, in the order
+    chain_run_blocks takes them: block c * nranks + rank for c = 0 .. blocks_per_rank - 1. The rows must
+    divide into nranks * blocks_per_rank blocks of equal size."""
+    row_ptr = np.asarray(row_ptr, dtype=np.int64)
+    rows = row_ptr.size - 1
+    blocks = nranks * blocks_per_rank
+    if rows % blocks:
+        raise ValueError(f"{rows} rows do not divide into {blocks} equal blocks")
+    block_rows = rows // blocks
+    out = []
+    for c in range(blocks_per_rank):
+        first = (c * nranks + rank) * block_rows
+        begin, end = int(row_ptr[first]), int(row_ptr[first + block_rows])
+        out.append(((row_ptr[first:first + block_rows + 1] - begin).astype(np.int32), col_ind[begin:end],
+                    values[begin:end]))
+    return out
 
 
 def exported_symbols() -> Sequence[str]:

@@ -1,7 +1,8 @@
 """Chained products over NCCL on two GPUs (spmv_chain_run): each rank's CSR-lp shard product into its
 slice of the next x, the slices all-gathered (grouped broadcasts for nnz-balanced shards of unequal rows,
-one all-gather for equal ones), three times; the result bit-identical to the oracle's chain on the whole
-matrix."""
+one all-gather for equal ones), three times; and over interleaved row blocks whose all-gathers run beside
+the next block's product (spmv_chain_run_blocks); the results bit-identical to the oracle's chain on the
+whole matrix."""
 import datetime
 import os
 import socket
@@ -53,6 +54,22 @@ def worker(rank, world, port):
             comm.check(stream, 30000)
             result = x_next.cpu().numpy()    # an odd count of products ends in x_next
         assert np.array_equal(result.view(np.uint64), expected.view(np.uint64)), bounds.tolist()
+    # interleaved row blocks (spmv_chain_run_blocks): 2 ranks x 4 blocks of 2500 rows; rank r holds blocks
+    # r, r + 2, r + 4, r + 6; an odd and an even count of products
+    blocks_per_rank, block_rows = 4, 2500
+    ops = [spmv.Operator(matrix.slice_rows((c * world + rank) * block_rows, (c * world + rank + 1) * block_rows),
+                         spmv.LP, spmv.F64, 8, device=rank) for c in range(blocks_per_rank)]
+    fourth = oracle.spmv_csr(row_ptr, col_ind, values, expected, spmv.F64, spmv.LP, 8)
+    for products, want in ((3, expected), (4, fourth)):
+        x_current = torch.from_numpy(x0).cuda()
+        x_next = torch.zeros_like(x_current)
+        stream = torch.cuda.current_stream().cuda_stream
+        spmv.chain_run_blocks(ops, block_rows, comm, x_current.data_ptr(), x_next.data_ptr(), products, stream)
+        comm.check(stream, 30000)
+        result = (x_next if products % 2 else x_current).cpu().numpy()
+        assert np.array_equal(result.view(np.uint64), want.view(np.uint64)), products
+    for op in ops:
+        op.close()
     comm.close()
     dist.destroy_process_group()
 
