@@ -19,10 +19,11 @@ cudaError_t launch_tiles_f64(int layout, int tpr, int physical_tpr, const Kernel
 cudaError_t launch_tiles_f32(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream);
 cudaError_t launch_tiles_f16(int layout, int tpr, int physical_tpr, const KernelArgs& a, cudaStream_t stream);
 // Resident k_spmv_tiles CTAs per multiprocessor with `smem` bytes of dynamic shared memory (0 if the
-// variant does not exist); also raises the kernel's shared-memory limit to smem.
-int tiles_occupancy_f64(int layout, int tpr, int physical_tpr, int smem);
-int tiles_occupancy_f32(int layout, int tpr, int physical_tpr, int smem);
-int tiles_occupancy_f16(int layout, int tpr, int physical_tpr, int smem);
+// variant does not exist); also raises the kernel's shared-memory limit to smem. dense: the dense variant
+// (KernelArgs::dense) where P = T.
+int tiles_occupancy_f64(int layout, int tpr, int physical_tpr, int smem, bool dense);
+int tiles_occupancy_f32(int layout, int tpr, int physical_tpr, int smem, bool dense);
+int tiles_occupancy_f16(int layout, int tpr, int physical_tpr, int smem, bool dense);
 // k_spmv_vector over `blocks` CTAs of kVectorBlock threads.
 cudaError_t launch_vector_f64(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream);
 cudaError_t launch_vector_f32(int layout, int tpr, const KernelArgs& a, int64_t blocks, cudaStream_t stream);
@@ -61,11 +62,11 @@ inline cudaError_t launch_tiles(int dtype, int layout, int tpr, int physical_tpr
   }
 }
 
-inline int tiles_occupancy(int dtype, int layout, int tpr, int physical_tpr, int smem) {
+inline int tiles_occupancy(int dtype, int layout, int tpr, int physical_tpr, int smem, bool dense) {
   switch (dtype) {
-    case SPMV_F64: return tiles_occupancy_f64(layout, tpr, physical_tpr, smem);
-    case SPMV_F32: return tiles_occupancy_f32(layout, tpr, physical_tpr, smem);
-    default:       return tiles_occupancy_f16(layout, tpr, physical_tpr, smem);
+    case SPMV_F64: return tiles_occupancy_f64(layout, tpr, physical_tpr, smem, dense);
+    case SPMV_F32: return tiles_occupancy_f32(layout, tpr, physical_tpr, smem, dense);
+    default:       return tiles_occupancy_f16(layout, tpr, physical_tpr, smem, dense);
   }
 }
 

@@ -107,6 +107,8 @@ struct KernelArgs {
   int long_chunk;            // k_spmv_tiles: entries per chunk of a long row (a multiple of kTileBlock)
   int smem_bytes;            // k_spmv_tiles: dynamic shared memory of the launch
   int64_t tile_ctas;         // k_spmv_tiles: persistent CTAs over the tiles after the vector blocks
+  int dense;                 // k_spmv_tiles with one thread per lane (P = T): the variant budgeted for more
+                             // CTAs per multiprocessor (kDenseResidency)
   unsigned* status;          // device status word (may be null)
   // k_spmv_classes (rows by length): long-row blocks, then the blocks of each segment of listed rows
   // (P = 32, 16, ..., 1 threads per row), then the short-row blocks
@@ -536,14 +538,22 @@ __device__ __forceinline__ typename ValueTraits<V>::Acc row_product(const View& 
 #endif
 constexpr int kGathers = SPMV_TILE_GATHERS;
 
-template <class V, int LAYOUT, int T, int P>
+// CTAs per multiprocessor whose registers a tile variant is built for: 2, or for the dense variants of one
+// thread per lane (P = T, not CSR-lp) 4 with 4-byte or narrower values and 3 with FP64 ones. A thread of a
+// dense variant gathers 8 x values at once (the lane's entries of a row up to 8*T long in one round trip).
+// Measured on B200 (block FEM, 64 nonzeros a row in runs of 8, FP32, T = 8): 0.86 of the measured peak
+// against 0.56 at 2 CTAs; rows with x windows (random band) lose their window room and run slower.
+template <class V>
+struct DenseResidency { static constexpr int value = sizeof(V) == 8 ? 3 : 4; };
+
+template <class V, int LAYOUT, int T, int P, int W>
 __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned char* stage, const StagePlan& plan) {
   using VT = ValueTraits<V>;
   constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
   constexpr int S = T / P;
   // x values gathered at once per thread: 32, or 16 for FP64 when 16 lane sums (or 8 CSR-lp lanes with
   // their running columns) already hold many of the 128 registers two CTAs of 256 threads leave a thread
-  constexpr int kBatch = (sizeof(V) == 8 && (S >= 16 || (kPacked && S >= 8))) ? kGathers / 2 : kGathers;
+  constexpr int kBatch = W > 2 ? 8 : ((sizeof(V) == 8 && (S >= 16 || (kPacked && S >= 8))) ? kGathers / 2 : kGathers);
   constexpr int kGroups = kTileBlock / P;
   const TileView<V, LAYOUT> tile(stage, plan);
   const V* x = static_cast<const V*>(a.x);
@@ -950,8 +960,9 @@ __global__ void __launch_bounds__(kTileBlock, 4) k_spmv_classes(const KernelArgs
 // Per tile k (buffer s = k mod stages): every thread waits for the buffer's bulk copies and processes its
 // rows; each warp then counts itself out of the buffer, and the last warp out refills it at once with
 // tile k + stages. No warp ever waits for another, nor for a producer.
-template <class V, int LAYOUT, int T, int P>
-__global__ void __launch_bounds__(kTileBlock, 2) k_spmv_tiles(const KernelArgs a) {
+// W: the CTAs per multiprocessor the registers are budgeted for (2, or DenseResidency for dense variants).
+template <class V, int LAYOUT, int T, int P, int W>
+__global__ void __launch_bounds__(kTileBlock, W) k_spmv_tiles(const KernelArgs a) {
   static_assert(T % P == 0 && P >= 1 && P <= 32, "P must divide T");
   constexpr int kWarps = kTileBlock / 32;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -993,7 +1004,7 @@ __global__ void __launch_bounds__(kTileBlock, 2) k_spmv_tiles(const KernelArgs a
     }
     // leave together or not at all: the reduction's shuffles need every lane of the warp
     if (__shfl_sync(0xffffffffu, *(volatile int*)&s_abort, 0)) break;
-    process_tile<V, LAYOUT, T, P>(a, buffers + s * plan.bytes, plan);
+    process_tile<V, LAYOUT, T, P, W>(a, buffers + s * plan.bytes, plan);
     __syncwarp();
     if ((threadIdx.x & 31) == 0) {
       __threadfence_block();   // this warp's reads of the buffer happen before its release

@@ -5,33 +5,36 @@
 namespace spmvb200 {
 namespace {
 
-template <class V, int L, int T, int P>
+template <class V, int L, int T, int P, int W>
 cudaError_t run_tiles(const KernelArgs& a, cudaStream_t stream) {
   const int smem = a.smem_bytes;
   const int64_t blocks = a.vector_blocks + a.tile_ctas;
   if (blocks <= 0) return cudaSuccess;
-  k_spmv_tiles<V, L, T, P><<<(unsigned)blocks, kTileBlock, smem, stream>>>(a);
+  k_spmv_tiles<V, L, T, P, W><<<(unsigned)blocks, kTileBlock, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
 // Sets the shared-memory limit of the variant to smem and returns its resident CTAs per multiprocessor.
-template <class V, int L, int T, int P>
+template <class V, int L, int T, int P, int W>
 cudaError_t occupancy_of(int smem, int* blocks) {
-  cudaError_t status = cudaFuncSetAttribute(k_spmv_tiles<V, L, T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t status = cudaFuncSetAttribute(k_spmv_tiles<V, L, T, P, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (status != cudaSuccess) return status;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k_spmv_tiles<V, L, T, P>, kTileBlock, smem);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k_spmv_tiles<V, L, T, P, W>, kTileBlock, smem);
 }
 
 // mode 0: launch; mode 1: occupancy query into *blocks
-template <class V, int L, int T, int P>
+template <class V, int L, int T, int P, int W = 2>
 cudaError_t tiles_variant(int mode, const KernelArgs& a, cudaStream_t stream, int smem, int* blocks) {
-  return mode == 0 ? run_tiles<V, L, T, P>(a, stream) : occupancy_of<V, L, T, P>(smem, blocks);
+  return mode == 0 ? run_tiles<V, L, T, P, W>(a, stream) : occupancy_of<V, L, T, P, W>(smem, blocks);
 }
 
 template <class V, int L, int T>
 cudaError_t tiles_for_tpr(int physical_tpr, int mode, const KernelArgs& a, cudaStream_t stream, int smem, int* blocks) {
   switch (T / physical_tpr) {
-    case 1: return tiles_variant<V, L, T, T>(mode, a, stream, smem, blocks);
+    case 1:
+      if constexpr (L != SPMV_LAYOUT_LP)
+        if (a.dense) return tiles_variant<V, L, T, T, DenseResidency<V>::value>(mode, a, stream, smem, blocks);
+      return tiles_variant<V, L, T, T>(mode, a, stream, smem, blocks);
     case 2: if constexpr (T >= 2) return tiles_variant<V, L, T, T / 2>(mode, a, stream, smem, blocks); break;
     case 4: if constexpr (T >= 4) return tiles_variant<V, L, T, T / 4>(mode, a, stream, smem, blocks); break;
     case 8: if constexpr (T >= 8) return tiles_variant<V, L, T, T / 8>(mode, a, stream, smem, blocks); break;
@@ -136,10 +139,11 @@ cudaError_t LAUNCH_TILES_NAME(int layout, int tpr, int physical_tpr, const Kerne
   return tiles_for_value<VALUE_TYPE>(layout, tpr, physical_tpr, 0, a, stream, 0, nullptr);
 }
 
-int TILES_OCCUPANCY_NAME(int layout, int tpr, int physical_tpr, int smem) {
+int TILES_OCCUPANCY_NAME(int layout, int tpr, int physical_tpr, int smem, bool dense) {
   int blocks = 0;
-  const KernelArgs unused{};
-  if (tiles_for_value<VALUE_TYPE>(layout, tpr, physical_tpr, 1, unused, nullptr, smem, &blocks) != cudaSuccess) return 0;
+  KernelArgs variant{};
+  variant.dense = dense ? 1 : 0;
+  if (tiles_for_value<VALUE_TYPE>(layout, tpr, physical_tpr, 1, variant, nullptr, smem, &blocks) != cudaSuccess) return 0;
   return blocks;
 }
 

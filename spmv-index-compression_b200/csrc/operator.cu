@@ -275,6 +275,7 @@ struct spmv_operator {
   int2* tile_windows = nullptr;   // tiles: the x window each tile stages, {first, end} column (first == end: none)
   int window_elements = 0;
   int resident = 1;   // tiles: persistent CTAs per multiprocessor
+  bool dense = false; // tiles: the dense variant (one thread per lane, more CTAs per multiprocessor)
   int64_t segment_first[6] = {0, 0, 0, 0, 0, 0};
   int64_t segment_items[6] = {0, 0, 0, 0, 0, 0};
   int64_t segment_blocks[6] = {0, 0, 0, 0, 0, 0};
@@ -320,6 +321,7 @@ KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   a.window_elements = op->window_elements;
   a.stages = op->stages;
   a.tile_ctas = op->tile_ctas;
+  a.dense = op->dense ? 1 : 0;
   a.row_list = op->long_rows;
   a.row_count = op->long_count;
   a.vector_blocks = op->long_ctas;
@@ -541,7 +543,10 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
       const double row_nnz = (double)op->tile_rows * std::max(1.0, mean_length) * 1.125;
       op->tile_nnz = std::max(256, std::min(8192, ((int)row_nnz + 255) / 256 * 256));
     }
-    const int register_ctas = std::max(1, tiles_occupancy(dtype, layout, tpr, op->physical_tpr, 0));
+    // the dense variant where one thread holds one lane (P = T) and the gathers come in runs: its x never
+    // takes a window, so the shared memory goes to more CTAs per multiprocessor instead
+    op->dense = op->physical_tpr == tpr && !packed && run_length >= 1.5;
+    const int register_ctas = std::max(1, tiles_occupancy(dtype, layout, tpr, op->physical_tpr, 0, op->dense));
     const int budget = per_sm / register_ctas - 1024 - 1024;   // per CTA: minus reserved and static shared memory
     auto plan_for = [&](int tile_nnz) {
       return plan_tiles(m, tile_nnz, op->tile_rows, packed ? row_word.data() : nullptr, packed ? row_width.data() : nullptr);
@@ -596,7 +601,7 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     op->smem_bytes = std::max(smem, op->long_count > 0 ? long_smem_bytes(op->long_chunk, value_bytes, packed) : 0);
     if (op->smem_bytes > shared_limit) fail(SPMV_ERR_INVALID_ARGUMENT, "long-row chunk exceeds the shared memory of a block");
     // persistent tile CTAs: as many as fit on the device at once, never more than there are tiles
-    const int resident = tiles_occupancy(dtype, layout, tpr, op->physical_tpr, op->smem_bytes);
+    const int resident = tiles_occupancy(dtype, layout, tpr, op->physical_tpr, op->smem_bytes, op->dense);
     if (resident <= 0 && (op->tile_count > 0 || op->long_count > 0))
       fail(SPMV_ERR_CUDA, "tile kernel cannot be resident with this configuration");
     op->resident = std::max(1, resident);

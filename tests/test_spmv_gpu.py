@@ -341,6 +341,24 @@ def test_run_host_batch_pipelines_a_stream_of_vectors(ragged):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
+def test_dense_variants_one_thread_per_lane(dtype):
+    """One thread per lane (P = T) on gathers in runs: the dense tile variants (4 CTAs a multiprocessor, 3
+    for FP64, 8 gathers at once) at every T, bit-identical to the oracle, with more persistent CTAs than
+    the 2 a multiprocessor of the other variants."""
+    matrix = spmv.synth_block_fem(60000, 8, 8, 2000, 4, 0, 60000)   # i16: at most 65536 columns
+    x = spmv.fill_uniform(dtype, matrix.cols, 8)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    for layout in (spmv.I32, spmv.I16, spmv.R16):
+        for tpr in spmv.THREADS_PER_ROW:
+            with spmv.Operator(matrix, layout, dtype, tpr, physical_tpr=tpr) as op:
+                info = op.info()
+                assert info.tile_ctas == min(info.tiles, (3 if dtype == spmv.F64 else 4) * sms), (layout, tpr)
+                y = device_run(op, x)
+            assert np.array_equal(bits(y), bits(oracle_product(matrix, x, dtype, layout, tpr))), \
+                (spmv.LAYOUT_NAMES[layout], tpr)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
 def test_block_rows_of_column_runs(dtype):
     """8x8-block rows (64 nonzeros in runs of 8 columns): 8 threads a row, two 32-row passes a tile; every
     layout bit-identical to the oracle."""
