@@ -58,6 +58,8 @@ def parse_args():
     parser.add_argument("--tpr", type=int, default=8)
     parser.add_argument("--physical-tpr", type=int, default=0)
     parser.add_argument("--tile-nnz", type=int, default=0)
+    parser.add_argument("--fem-rows", type=int, default=FEM_ROWS,
+                        help="fem: n of the block-FEM matrix (a multiple of 8; smaller n for profiling captures)")
     parser.add_argument("--blocks-per-rank", type=int, default=0,
                         help="fem: interleaved row blocks per rank whose all-gathers overlap the next block's "
                              "product (0: 4 on more than one GPU, else 1; 1: one shard and spmv_chain_run)")
@@ -211,7 +213,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     if args.workload == "fem":   # a row range of the 2.05 G-nonzero matrix stands in (host memory)
-        matrix = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, 0, 2_000_000)
+        matrix = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, 0, min(FEM_ROWS, 2_000_000))
     else:
         matrix = build_matrix(spmv, args.workload)
     dtype_code = spmv.DTYPE_BY_NAME[DTYPE_OF[args.workload]]
@@ -515,7 +517,8 @@ def run_fem(args, rank, world, local_rank):
         "metric": METRIC, "value": round(2.0 * total_nnz * args.steps / (elapsed_ms * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": WORKLOADS["fem"], "layout": args.layout, "tpr": args.tpr, "rows": FEM_ROWS,
+        "config": {"workload": WORKLOADS["fem"].replace("n=32M", f"n={FEM_ROWS}") if FEM_ROWS != 32_000_000
+                   else WORKLOADS["fem"], "layout": args.layout, "tpr": args.tpr, "rows": FEM_ROWS,
                    "nnz": total_nnz, "parallelism": parallelism,
                    "l2": f"no flush: {algorithmic_bytes / 1e9:.2f} GB per rank > 126 MB L2",
                    "physical_tpr": info.physical_tpr, "tile_nnz": info.tile_nnz,
@@ -586,7 +589,11 @@ def sweep(args, torch, spmv, matrix, dtype_code, torch_dtype, x, stream):
 
 
 def main():
+    global FEM_ROWS
     args = parse_args()
+    if args.fem_rows <= 0 or args.fem_rows % 8:
+        raise SystemExit("--fem-rows must be a positive multiple of 8")
+    FEM_ROWS = args.fem_rows
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -539,10 +539,11 @@ __device__ __forceinline__ typename ValueTraits<V>::Acc row_product(const View& 
 constexpr int kGathers = SPMV_TILE_GATHERS;
 
 // CTAs per multiprocessor whose registers a tile variant is built for: 2, or for the dense variants of one
-// thread per lane (P = T, not CSR-lp) 4 with 4-byte or narrower values and 3 with FP64 ones. A thread of a
-// dense variant gathers 8 x values at once (the lane's entries of a row up to 8*T long in one round trip).
-// Measured on B200 (block FEM, 64 nonzeros a row in runs of 8, FP32, T = 8): 0.86 of the measured peak
-// against 0.56 at 2 CTAs; rows with x windows (random band) lose their window room and run slower.
+// thread per lane (P = T) 4 with 4-byte or narrower values and 3 with FP64 ones. A thread of a dense
+// variant gathers 8 x values at once (the lane's entries of a row up to 8*T long in one round trip).
+// Measured on B200 (block FEM slice, 64 nonzeros a row in runs of 8, FP32, T = 8): 208 us a product
+// against 321 us at 2 CTAs (CSR-lp: 236 us against 365 us with P = 4); rows with x windows (random band)
+// lose their window room and run slower.
 template <class V>
 struct DenseResidency { static constexpr int value = sizeof(V) == 8 ? 3 : 4; };
 

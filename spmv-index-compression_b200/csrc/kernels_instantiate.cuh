@@ -32,8 +32,7 @@ template <class V, int L, int T>
 cudaError_t tiles_for_tpr(int physical_tpr, int mode, const KernelArgs& a, cudaStream_t stream, int smem, int* blocks) {
   switch (T / physical_tpr) {
     case 1:
-      if constexpr (L != SPMV_LAYOUT_LP)
-        if (a.dense) return tiles_variant<V, L, T, T, DenseResidency<V>::value>(mode, a, stream, smem, blocks);
+      if (a.dense) return tiles_variant<V, L, T, T, DenseResidency<V>::value>(mode, a, stream, smem, blocks);
       return tiles_variant<V, L, T, T>(mode, a, stream, smem, blocks);
     case 2: if constexpr (T >= 2) return tiles_variant<V, L, T, T / 2>(mode, a, stream, smem, blocks); break;
     case 4: if constexpr (T >= 4) return tiles_variant<V, L, T, T / 4>(mode, a, stream, smem, blocks); break;

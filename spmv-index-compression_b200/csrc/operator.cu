@@ -428,11 +428,18 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     const double run_length = entries_per_x_sector(m, value_bytes);
     op->physical_tpr = config->physical_tpr > 0 ? config->physical_tpr : choose_physical_tpr(tpr, layout, mean_length);
     op->tile_rows = config->tile_rows > 0 ? config->tile_rows : std::max(128, kTileBlock / op->physical_tpr);
-    // long rows of column runs (at least 4 nonzeros per x sector, as in block matrices): 8 threads a row read
-    // 8 consecutive columns of a run together, and a tile is two passes of 32 rows. Measured on B200 (block
-    // FEM, 64 nonzeros a row in runs of 8, FP32): 0.53 of the measured peak against 0.47 with P = 4.
-    if (config->physical_tpr == 0 && config->tile_rows == 0 && run_length >= 4.0 && mean_length >= 32.0 &&
-        layout != SPMV_LAYOUT_LP && tpr >= 8) {
+    // long rows of column runs (at least 4 nonzeros per x sector, as in block matrices): one thread per
+    // lane up to T = 16 (the dense variant: consecutive lanes read consecutive columns of a run together),
+    // else 8 threads a row (not CSR-lp); a tile is at least two passes. Measured on B200 (block-FEM slice,
+    // 64 nonzeros a row in runs of 8, FP32, CSR-i32): T = 8 208 us a product (P = 8 dense) against 321 us
+    // (P = 8, 2 CTAs an SM) and 0.47 of the peak with P = 4; T = 16 240 us (P = 16) against 321 us (P = 8);
+    // T = 32 326 us with P = 8 against 364 us with P = 32.
+    const bool column_runs = config->physical_tpr == 0 && config->tile_rows == 0 && run_length >= 4.0 &&
+                             mean_length >= 32.0 && tpr >= 8;
+    if (column_runs && tpr <= 16) {
+      op->physical_tpr = tpr;
+      op->tile_rows = std::max(64, 2 * kTileBlock / op->physical_tpr);
+    } else if (column_runs && layout != SPMV_LAYOUT_LP) {
       op->physical_tpr = std::max(op->physical_tpr, 8);
       op->tile_rows = 2 * kTileBlock / op->physical_tpr;
     }
@@ -545,7 +552,7 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     }
     // the dense variant where one thread holds one lane (P = T) and the gathers come in runs: its x never
     // takes a window, so the shared memory goes to more CTAs per multiprocessor instead
-    op->dense = op->physical_tpr == tpr && !packed && run_length >= 1.5;
+    op->dense = op->physical_tpr == tpr && run_length >= 1.5;
     const int register_ctas = std::max(1, tiles_occupancy(dtype, layout, tpr, op->physical_tpr, 0, op->dense));
     const int budget = per_sm / register_ctas - 1024 - 1024;   // per CTA: minus reserved and static shared memory
     auto plan_for = [&](int tile_nnz) {

@@ -348,7 +348,7 @@ def test_dense_variants_one_thread_per_lane(dtype):
     matrix = spmv.synth_block_fem(60000, 8, 8, 2000, 4, 0, 60000)   # i16: at most 65536 columns
     x = spmv.fill_uniform(dtype, matrix.cols, 8)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    for layout in (spmv.I32, spmv.I16, spmv.R16):
+    for layout in (spmv.I32, spmv.I16, spmv.R16, spmv.LP):
         for tpr in spmv.THREADS_PER_ROW:
             with spmv.Operator(matrix, layout, dtype, tpr, physical_tpr=tpr) as op:
                 info = op.info()
@@ -360,13 +360,15 @@ def test_dense_variants_one_thread_per_lane(dtype):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 def test_block_rows_of_column_runs(dtype):
-    """8x8-block rows (64 nonzeros in runs of 8 columns): 8 threads a row, two 32-row passes a tile; every
-    layout bit-identical to the oracle."""
+    """8x8-block rows (64 nonzeros in runs of 8 columns): one thread per lane up to T = 16, else 8 threads a
+    row (not CSR-lp), at least two passes a tile; every layout bit-identical to the oracle."""
     matrix = spmv.synth_block_fem(20000, 8, 8, 2000, 4, 0, 20000)
     x = spmv.fill_uniform(dtype, matrix.cols, 6)
-    for layout, tpr in ((spmv.I32, 8), (spmv.R16, 16), (spmv.I16, 32), (spmv.LP, 8)):
+    for layout, tpr in ((spmv.I32, 8), (spmv.R16, 16), (spmv.I16, 32), (spmv.LP, 8), (spmv.LP, 16), (spmv.LP, 32)):
         with spmv.Operator(matrix, layout, dtype, tpr) as op:
-            if layout != spmv.LP:
+            if tpr <= 16:
+                assert op.info().physical_tpr == tpr and op.info().tile_rows == 64
+            elif layout != spmv.LP:
                 assert op.info().physical_tpr == 8 and op.info().tile_rows == 64
             y = device_run(op, x)
         assert np.array_equal(bits(y), bits(oracle_product(matrix, x, dtype, layout, tpr))), (spmv.LAYOUT_NAMES[layout], tpr)
