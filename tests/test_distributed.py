@@ -1,6 +1,7 @@
 """The multi-GPU host logic on CPU ranks (gloo, world size 2): nnz-balanced row shards, each rank's shard
 product (the oracle stands in for the GPU), the all-gather of unequal shards into the next x, chained
-products, and a rank that leaves before a collective being detected by the other rank's timeout."""
+products, the interleaved row blocks whose rounds are all-gathered one by one, and a rank that leaves
+before a collective being detected by the other rank's timeout."""
 import datetime
 import os
 import socket
@@ -60,6 +61,33 @@ def chained_worker(rank, world, port):
     dist.destroy_process_group()
 
 
+def interleaved_worker(rank, world, port):
+    """spmv_chain_run_blocks' exchange: rank r holds blocks c * world + r; after each of its blocks, the
+    round of blocks c * world .. c * world + world - 1 is all-gathered into its place in the next x."""
+    setup(rank, world, port)
+    import oracle
+    import spmvb200 as spmv
+    blocks_per_rank, block_rows = 3, 500
+    n = world * blocks_per_rank * block_rows
+    matrix = spmv.synth_random_band(n, 200, 9.0, 2)
+    row_ptr, col_ind, values = matrix.arrays()
+    mine = spmv.interleaved_block_rows(row_ptr, col_ind, values, world, blocks_per_rank, rank)
+    x = spmv.fill_uniform(spmv.F64, n, 6)
+    expected = x.copy()
+    for _ in range(3):
+        expected = oracle.spmv_csr(row_ptr, col_ind, values, expected, spmv.F64, spmv.LP, 8)
+        x_next = np.zeros_like(x)
+        for c, (b_ptr, b_col, b_val) in enumerate(mine):
+            y_block = oracle.spmv_csr(b_ptr, b_col, b_val, x, spmv.F64, spmv.LP, 8)
+            pieces = [torch.zeros(block_rows, dtype=torch.float64) for _ in range(world)]
+            dist.all_gather(pieces, torch.from_numpy(y_block))
+            first = c * world * block_rows
+            x_next[first:first + world * block_rows] = np.concatenate([piece.numpy() for piece in pieces])
+        x = x_next
+    assert np.array_equal(x.view(np.uint64), expected.view(np.uint64))
+    dist.destroy_process_group()
+
+
 def leaving_worker(rank, world, port):
     setup(rank, world, port, seconds=5)
     if rank == 1:
@@ -73,6 +101,10 @@ def leaving_worker(rank, world, port):
 
 def test_sharded_chained_products_match_the_whole_matrix():
     mp.spawn(chained_worker, args=(2, free_port()), nprocs=2, join=True)
+
+
+def test_interleaved_row_blocks_match_the_whole_matrix():
+    mp.spawn(interleaved_worker, args=(2, free_port()), nprocs=2, join=True)
 
 
 def test_a_rank_that_leaves_is_detected_by_timeout():
