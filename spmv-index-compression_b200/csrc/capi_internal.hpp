@@ -1,5 +1,7 @@
-// capi_internal.hpp — error plumbing shared by the C entry points.
+// capi_internal.hpp — error plumbing and internals shared by the C entry points.
 #pragma once
+
+#include <cuda_runtime.h>
 
 #include <functional>
 #include <memory>
@@ -16,5 +18,8 @@ int guarded(const std::function<void()>& body);
 void require(bool condition, const char* message);
 // The caller's facts, or facts_of(matrix) when facts is null.
 Facts facts_for(const spmv_csr* matrix, const spmv_facts* facts);
+// One product on `stream` whose tile kernel launches free_sms multiprocessors' worth of persistent CTAs
+// fewer, so that kernels running beside it (collectives) find free multiprocessors (operator.cu).
+cudaError_t run_operator_leaving_sms(const spmv_operator* op, const void* x, void* y, cudaStream_t stream, int free_sms);
 
 }  // namespace spmvb200

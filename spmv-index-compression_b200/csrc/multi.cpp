@@ -90,9 +90,6 @@ struct spmv_comm {
   cudaStream_t side = nullptr;   // the all-gathers of spmv_chain_run_blocks, beside the products
 };
 
-namespace spmvb200 {
-cudaError_t run_operator_leaving_sms(const spmv_operator* op, const void* x, void* y, cudaStream_t stream, int free_sms);
-}
 
 using namespace spmvb200;
 
@@ -232,10 +229,15 @@ int spmv_chain_run_blocks(const spmv_operator* const* block_ops, int blocks_per_
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     NcclApi& api = nccl();
     if (!comm->side) {
-      const cudaError_t created = cudaStreamCreateWithFlags(&comm->side, cudaStreamNonBlocking);
+      // the side stream lives on the communicator's device, whichever device is current
+      int previous = 0;
+      cudaError_t created = cudaGetDevice(&previous);
+      if (created == cudaSuccess && previous != comm->device) created = cudaSetDevice(comm->device);
+      if (created == cudaSuccess) created = cudaStreamCreateWithFlags(&comm->side, cudaStreamNonBlocking);
+      if (previous != comm->device) cudaSetDevice(previous);
       if (created != cudaSuccess) {
         comm->side = nullptr;
-        fail(SPMV_ERR_CUDA, std::string("cudaStreamCreateWithFlags: ") + cudaGetErrorString(created));
+        fail(SPMV_ERR_CUDA, std::string("side stream: ") + cudaGetErrorString(created));
       }
     }
     // computed[c]: block c's product of the current x is in place; computed[blocks_per_rank]: the last round
