@@ -202,7 +202,14 @@ typedef struct {
   int stages;             /* shared-memory tile buffers per CTA, 1..4 (0 = default)                  */
   int tile_rows;          /* rows a tile holds at most, a multiple of 16 (0 = chosen by the library)  */
   int schedule;           /* SPMV_SCHEDULE_*: how rows are mapped to the kernel (0 = chosen by the library) */
+  int accumulate;         /* SPMV_ACCUMULATE_*: the type FP16 values are summed in (0 = FP32)             */
 } spmv_operator_config;
+
+/* The type a product sums in. WIDE: FP64 values in FP64, FP32 and FP16 values in FP32 (AccumulatorOf,
+ * value_types.cuh:9-13; the reference's campaign build). HALF: FP16 values summed in FP16, one __hfma
+ * per entry and one __hadd per step of the lane tree, the reference's SPMV_HALF_ACCUMULATE control
+ * build (value_types.cuh:7-33, CMakeLists.txt:32); FP16 operators only. */
+enum { SPMV_ACCUMULATE_WIDE = 0, SPMV_ACCUMULATE_HALF = 1 };
 
 /* Row schedules. Tiles: runs of consecutive rows staged in shared memory (rows of similar lengths).
  * Classes: rows grouped by length, each group on its own thread mapping straight from global memory
@@ -210,7 +217,7 @@ typedef struct {
 enum { SPMV_SCHEDULE_AUTO = 0, SPMV_SCHEDULE_TILES = 1, SPMV_SCHEDULE_CLASSES = 2 };
 
 /* Fills a config with defaults: physical_tpr 0, tile_nnz 0, value_rounding 0, device -1, stages 0,
- * tile_rows 0, schedule SPMV_SCHEDULE_AUTO. */
+ * tile_rows 0, schedule SPMV_SCHEDULE_AUTO, accumulate SPMV_ACCUMULATE_WIDE. */
 void spmv_operator_config_init(spmv_operator_config* config, int layout, int dtype, int tpr);
 
 /* upload_matrix + upload_* (bench_csr_width.cu:795-951): encodes the matrix in the layout, converts

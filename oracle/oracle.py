@@ -21,7 +21,9 @@ REFERENCE_CHARACTERIZE = os.path.join(HERE, "_ref", "characterize_matrix")
 
 I32, I16, R16, LP, I8, R8 = 0, 1, 2, 3, 4, 5
 F64, F32, F16 = 0, 1, 2
-NUMPY = {F64: np.float64, F32: np.float32, F16: np.float16}
+# F16_HALF_SUMS: FP16 values summed in FP16 (the reference's SPMV_HALF_ACCUMULATE control build)
+F16_HALF_SUMS = 3
+NUMPY = {F64: np.float64, F32: np.float32, F16: np.float16, F16_HALF_SUMS: np.float16}
 
 
 def build(reference: bool = False):
@@ -38,6 +40,7 @@ def _load_oracle():
     v, i, i64, d = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_double
     lib.oracle_spmv.restype = i
     lib.oracle_spmv.argtypes = [i, i, i, i, v, v, v, v, v, v, v, v, v, i]
+    lib.oracle_half_fma_array.argtypes = [i64, v, v, v, v]
     lib.oracle_lane_packed_words.restype = i64
     lib.oracle_lane_packed_words.argtypes = [i, v, v, i]
     lib.oracle_build_lane_packed.restype = i
@@ -188,6 +191,14 @@ def encode(row_ptr, col_ind, layout: int, tpr: int) -> dict:
                 "row_base": row_bases(row_ptr, col_ind)}
     row_word, row_width, words = build_lane_packed(row_ptr, col_ind, tpr)
     return {"row_base": row_bases(row_ptr, col_ind), "row_word": row_word, "row_width": row_width, "words": words}
+
+
+def half_fma(a, b, c) -> np.ndarray:
+    """a*b + c of FP16 arrays, rounded once to FP16 (what __hfma computes), element by element."""
+    a, b, c = (np.ascontiguousarray(t, np.float16) for t in (a, b, c))
+    out = np.zeros(max(a.size, 1), np.float16)
+    _oracle.oracle_half_fma_array(a.size, _p(a), _p(b), _p(c), _p(out))
+    return out[:a.size]
 
 
 def spmv_csr(row_ptr, col_ind, values64, x, dtype: int, layout: int, tpr: int, threads: int = 0) -> np.ndarray:

@@ -12,6 +12,8 @@
  *     the entries L, L+T, L+2T, ... with one fused multiply-add each, in the accumulator type
  *     (FP64 for FP64, FP32 for FP32 and FP16), and the T lane sums are then combined in the order
  *     of the __shfl_down_sync tree (offsets T/2, ..., 1), lane 0 narrowing the result;
+ *     With FP16 summed in FP16 (the SPMV_HALF_ACCUMULATE control build, value_types.cuh:7-33) every
+ *     multiply-add is one correctly rounded FP16 fma (__hfma) and every step of the tree one FP16 add;
  *   - the layout encoders (16/8-bit absolute columns, row-base offsets, the lane-packed delta
  *     stream), the admissibility tests and the byte model memory_of.
  *
@@ -28,7 +30,7 @@
 #include <omp.h>
 #endif
 
-enum { O_F64 = 0, O_F32 = 1, O_F16 = 2 };
+enum { O_F64 = 0, O_F32 = 1, O_F16 = 2, O_F16_HALF_SUMS = 3 };
 enum { O_I32 = 0, O_I16 = 1, O_R16 = 2, O_LP = 3, O_I8 = 4, O_R8 = 5 };
 
 /* ---------------------------------------------------------------------------------------------
@@ -307,6 +309,100 @@ static float row_f32(int dtype, int layout, int tpr, int row, const int* row_ptr
   return lane_sum[0];
 }
 
+/* ---------------------------------------------------------------------------------------------
+ * FP16 arithmetic rounded once, round to nearest even (the IEEE 754 binary16 fma and add that
+ * __hfma and __hadd compute), restated from the definition:
+ *   - a*b of two FP16 values is exact in FP64 (11-bit significands, exponents from 2^-48 to 2^32);
+ *   - s = fl64(a*b + c) and its error e (Knuth's TwoSum, exact: a*b + c = s + e);
+ *   - the FP16 rounding of a*b + c is that of s, except where s lies exactly halfway between two
+ *     FP16 values and e != 0: the exact value is then on e's side of the midpoint.
+ *   (No other double rounding can occur: every FP16 midpoint is an FP64 value, and s is the FP64
+ *   value nearest the exact sum, so the exact sum and s are never on different sides of a midpoint
+ *   that s does not equal.) The sum of two FP16 values is exact in FP64, so the add rounds once.
+ * ------------------------------------------------------------------------------------------- */
+
+/* The FP16 value next to h towards +inf (up) or -inf, by its bit pattern. */
+static _Float16 half_step(_Float16 h, int up) {
+  uint16_t bits;
+  memcpy(&bits, &h, sizeof bits);
+  if ((bits & 0x7fffu) == 0) bits = up ? 0x0001u : 0x8001u;
+  else if (!(bits & 0x8000u)) bits = (uint16_t)(up ? bits + 1 : bits - 1);
+  else bits = (uint16_t)(up ? bits - 1 : bits + 1);
+  memcpy(&h, &bits, sizeof bits);
+  return h;
+}
+
+_Float16 oracle_half_fma(_Float16 a, _Float16 b, _Float16 c) {
+  const double p = (double)a * (double)b, q = (double)c;
+  const double s = p + q;
+  const double t = s - p;
+  const double e = (p - (s - t)) + (q - t);
+  const _Float16 h = (_Float16)s;
+  if (e == 0.0 || (double)h == s || isnan(s)) return h;
+  /* the FP16 values around s: h and its neighbour on the other side of s */
+  const int h_below = isinf((double)h) ? (s < 0.0) : ((double)h < s);
+  const _Float16 other = half_step(h, h_below);
+  const double low = h_below ? (double)h : (double)other, high = h_below ? (double)other : (double)h;
+  /* the midpoint; the one above 65504 (towards infinity) is 65520 */
+  double middle;
+  if (isinf(high)) middle = 65520.0;
+  else if (isinf(low)) middle = -65520.0;
+  else middle = 0.5 * (low + high);
+  if (s != middle) return h;
+  return e > 0.0 ? (h_below ? other : h) : (h_below ? h : other);
+}
+
+_Float16 oracle_half_add(_Float16 a, _Float16 b) { return (_Float16)((double)a + (double)b); }
+
+/* oracle_half_fma over arrays of FP16 bit patterns (for the tests' exact-arithmetic check). */
+void oracle_half_fma_array(int64_t count, const _Float16* a, const _Float16* b, const _Float16* c, _Float16* out) {
+  for (int64_t i = 0; i < count; ++i) out[i] = oracle_half_fma(a[i], b[i], c[i]);
+}
+
+/* One row with FP16 sums (__hfma per entry, __hadd per tree step), CSR-lp or a column array. */
+static _Float16 row_f16_half_sums(int layout, int tpr, int row, const int* row_ptr, const void* columns,
+                                  const int* row_base, const int* row_word, const uint8_t* row_width,
+                                  const uint32_t* words, const _Float16* values, const _Float16* x) {
+  _Float16 lane_sum[LANES_MAX];
+  const int begin = row_ptr[row], end = row_ptr[row + 1];
+  for (int lane = 0; lane < tpr; ++lane) {
+    _Float16 sum = (_Float16)0.0f;
+    if (layout == O_LP) {
+      const int length = end - begin, quotient = length / tpr, remainder = length - quotient * tpr;
+      const int mine = quotient + (lane < remainder ? 1 : 0);
+      const int width = row_width[row];
+      const uint64_t mask = width == 0 ? 0ull : (~0ull >> (64 - width));
+      const int64_t start_bit = (int64_t)width * ((int64_t)lane * quotient + (lane < remainder ? lane : remainder));
+      int64_t word = row_word[row] + (start_bit >> 5);
+      uint64_t window = (((uint64_t)words[word + 1] << 32) | words[word]) >> (start_bit & 31);
+      int available = 64 - (int)(start_bit & 31);
+      int64_t next_word = word + 2;
+      int column = row_base[row];
+      int64_t entry = begin + lane;
+      for (int taken = 0; taken < mine; ++taken) {
+        column += (int)(window & mask);
+        sum = oracle_half_fma(values[entry], x[column], sum);
+        window >>= width;
+        available -= width;
+        entry += tpr;
+        if (available < width) {
+          window |= (uint64_t)words[next_word] << available;
+          available += 32;
+          ++next_word;
+        }
+      }
+    } else {
+      const int base = (layout == O_R16 || layout == O_R8) ? row_base[row] : 0;
+      for (int64_t entry = begin + lane; entry < end; entry += tpr)
+        sum = oracle_half_fma(values[entry], x[column_of(layout, columns, base, entry)], sum);
+    }
+    lane_sum[lane] = sum;
+  }
+  for (int offset = tpr / 2; offset > 0; offset >>= 1)
+    for (int lane = 0; lane < offset; ++lane) lane_sum[lane] = oracle_half_add(lane_sum[lane], lane_sum[lane + offset]);
+  return lane_sum[0];
+}
+
 /*
  * y = A x in the reference order for one layout at one threads-per-row T.
  *   columns: int32 (i32), uint16 (i16, r16 offsets) or uint8 (i8, r8 offsets); unused for lp.
@@ -317,7 +413,7 @@ int oracle_spmv(int dtype, int layout, int tpr, int rows, const int* row_ptr, co
                 const int* row_base, const int* row_word, const uint8_t* row_width, const uint32_t* words,
                 const void* values, const void* x, void* y, int threads) {
   if (tpr != 1 && tpr != 2 && tpr != 4 && tpr != 8 && tpr != 16 && tpr != 32) return -1;
-  if (dtype < 0 || dtype > 2 || layout < 0 || layout > 5 || rows < 0) return -1;
+  if (dtype < 0 || dtype > 3 || layout < 0 || layout > 5 || rows < 0) return -1;
 #ifdef _OPENMP
   if (threads <= 0) threads = omp_get_max_threads();
 #pragma omp parallel for schedule(dynamic, 2048) num_threads(threads)
@@ -326,6 +422,9 @@ int oracle_spmv(int dtype, int layout, int tpr, int rows, const int* row_ptr, co
     if (dtype == O_F64) {
       ((double*)y)[row] = row_f64(layout, tpr, row, row_ptr, columns, row_base, row_word, row_width, words,
                                   (const double*)values, (const double*)x);
+    } else if (dtype == O_F16_HALF_SUMS) {
+      ((_Float16*)y)[row] = row_f16_half_sums(layout, tpr, row, row_ptr, columns, row_base, row_word, row_width,
+                                              words, (const _Float16*)values, (const _Float16*)x);
     } else {
       const float sum = row_f32(dtype, layout, tpr, row, row_ptr, columns, row_base, row_word, row_width,
                                 words, values, x);

@@ -69,6 +69,20 @@ template <> struct ValueTraits<__half> {
   __device__ static __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
 };
 
+// FP16 values summed in FP16 (the reference's SPMV_HALF_ACCUMULATE control build, value_types.cuh:7-33):
+// every product-add one __hfma, every step of the tree one __hadd, the result stored as it is. The
+// storage is __half's under a type of its own, so that the kernels instantiate a family for it.
+struct __align__(2) half16 {
+  __half h;
+};
+template <> struct ValueTraits<half16> {
+  using Acc = __half;
+  __device__ static __forceinline__ __half widen(half16 v) { return v.h; }
+  __device__ static __forceinline__ half16 narrow(__half a) { return half16{a}; }
+  __device__ static __forceinline__ __half fma(__half a, __half b, __half c) { return __hfma(a, b, c); }
+  __device__ static __forceinline__ __half add(__half a, __half b) { return __hadd(a, b); }
+};
+
 // ---- column layouts -----------------------------------------------------------------------------
 template <int LAYOUT> struct LayoutTraits;
 template <> struct LayoutTraits<SPMV_LAYOUT_I32> { using Index = int;      static constexpr bool kBase = false; };
@@ -224,6 +238,10 @@ template <>
 __device__ __forceinline__ uint8_t load_readonly<uint8_t>(const uint8_t* pointer) {
   return (uint8_t)__ldg(reinterpret_cast<const unsigned char*>(pointer));
 }
+template <>
+__device__ __forceinline__ half16 load_readonly<half16>(const half16* pointer) {
+  return half16{__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(pointer)))};
+}
 
 // L2 policies: x, gathered at random and reused across rows, is kept (evict_last); the matrix streams, read
 // once per product, leave L2 first (evict_first), so that they do not push x out.
@@ -257,6 +275,13 @@ __device__ __forceinline__ __half load_x<__half>(const __half* pointer, uint64_t
   unsigned short bits;
   asm("ld.global.nc.L2::cache_hint.b16 %0, [%1], %2;" : "=h"(bits) : "l"(pointer), "l"(policy));
   return __ushort_as_half(bits);
+}
+
+template <>
+__device__ __forceinline__ half16 load_x<half16>(const half16* pointer, uint64_t policy) {
+  unsigned short bits;
+  asm("ld.global.nc.L2::cache_hint.b16 %0, [%1], %2;" : "=h"(bits) : "l"(pointer), "l"(policy));
+  return half16{__ushort_as_half(bits)};
 }
 
 // A read-only load of a matrix stream element with an L2 cache policy (values and column indices).

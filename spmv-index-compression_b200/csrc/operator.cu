@@ -248,6 +248,8 @@ ClassPlan plan_classes(const Csr& matrix, int tpr, int long_threshold) {
 struct spmv_operator {
   int device = 0;
   int layout = 0, dtype = 0, tpr = 0, physical_tpr = 0, tile_nnz = 0, tile_rows = 0, stages = 0, tile_index_words = 0;
+  int kernel = 0;   // kernel family: dtype, or kKernelHalfSums (FP16 summed in FP16)
+  int accumulate = SPMV_ACCUMULATE_WIDE;
   int rows = 0, cols = 0;
   int64_t nnz = 0;
   spmv_memory memory{};
@@ -346,8 +348,8 @@ int64_t class_blocks(const spmv_operator* op) {
 
 cudaError_t launch_product(const spmv_operator* op, const KernelArgs& a, cudaStream_t stream) {
   if (op->schedule == SPMV_SCHEDULE_CLASSES)
-    return launch_classes(op->dtype, op->layout, op->tpr, a, class_blocks(op), op->smem_bytes, stream);
-  return launch_tiles(op->dtype, op->layout, op->tpr, op->physical_tpr, a, stream);
+    return launch_classes(op->kernel, op->layout, op->tpr, a, class_blocks(op), op->smem_bytes, stream);
+  return launch_tiles(op->kernel, op->layout, op->tpr, op->physical_tpr, a, stream);
 }
 
 }  // namespace
@@ -388,6 +390,12 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
             "physical_tpr must divide T with T / physical_tpr in {1, 2, 4, 8, 16}");
     require(config->tile_nnz == 0 || (config->tile_nnz >= 64 && config->tile_nnz <= 16384),
             "tile_nnz must be 0 or in [64, 16384]");
+    require(config->accumulate == SPMV_ACCUMULATE_WIDE || config->accumulate == SPMV_ACCUMULATE_HALF,
+            "accumulate must be SPMV_ACCUMULATE_WIDE or SPMV_ACCUMULATE_HALF");
+    require(config->accumulate == SPMV_ACCUMULATE_WIDE || dtype == SPMV_F16,
+            "SPMV_ACCUMULATE_HALF applies to FP16 values only");
+    // the kernel family: FP16 sums in FP16 have their own instantiation
+    const int kernel = config->accumulate == SPMV_ACCUMULATE_HALF ? kKernelHalfSums : dtype;
     int device_count = 0;
     if (cudaGetDeviceCount(&device_count) != cudaSuccess || device_count == 0)
       fail(SPMV_ERR_UNSUPPORTED, "no CUDA device");
@@ -419,6 +427,8 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     cuda_check(cudaGetDevice(&op->device), "cudaGetDevice");
     op->layout = layout;
     op->dtype = dtype;
+    op->kernel = kernel;
+    op->accumulate = config->accumulate;
     op->tpr = tpr;
     op->rows = m.rows;
     op->cols = m.cols;
@@ -535,7 +545,7 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
       blocks += op->short_blocks;
       if (blocks > 0x7fffffff)
         fail(SPMV_ERR_TOO_LARGE, "grid exceeds 2^31-1 blocks");
-      cuda_check(prepare_classes(dtype, layout, tpr, op->smem_bytes), "class kernel shared memory");
+      cuda_check(prepare_classes(kernel, layout, tpr, op->smem_bytes), "class kernel shared memory");
       cuda_check(cudaDeviceSynchronize(), "operator upload");
       *out = op.release();
       return;
@@ -553,7 +563,7 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     // the dense variant where one thread holds one lane (P = T) and the gathers come in runs: its x never
     // takes a window, so the shared memory goes to more CTAs per multiprocessor instead
     op->dense = op->physical_tpr == tpr && run_length >= 1.5;
-    const int register_ctas = std::max(1, tiles_occupancy(dtype, layout, tpr, op->physical_tpr, 0, op->dense));
+    const int register_ctas = std::max(1, tiles_occupancy(kernel, layout, tpr, op->physical_tpr, 0, op->dense));
     const int budget = per_sm / register_ctas - 1024 - 1024;   // per CTA: minus reserved and static shared memory
     auto plan_for = [&](int tile_nnz) {
       return plan_tiles(m, tile_nnz, op->tile_rows, packed ? row_word.data() : nullptr, packed ? row_width.data() : nullptr);
@@ -608,7 +618,7 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     op->smem_bytes = std::max(smem, op->long_count > 0 ? long_smem_bytes(op->long_chunk, value_bytes, packed) : 0);
     if (op->smem_bytes > shared_limit) fail(SPMV_ERR_INVALID_ARGUMENT, "long-row chunk exceeds the shared memory of a block");
     // persistent tile CTAs: as many as fit on the device at once, never more than there are tiles
-    const int resident = tiles_occupancy(dtype, layout, tpr, op->physical_tpr, op->smem_bytes, op->dense);
+    const int resident = tiles_occupancy(kernel, layout, tpr, op->physical_tpr, op->smem_bytes, op->dense);
     if (resident <= 0 && (op->tile_count > 0 || op->long_count > 0))
       fail(SPMV_ERR_CUDA, "tile kernel cannot be resident with this configuration");
     op->resident = std::max(1, resident);

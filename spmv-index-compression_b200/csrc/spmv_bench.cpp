@@ -4,6 +4,7 @@
 //
 //   spmv_bench --matrix A.mtx [--matrix B.mtx ...] [--reps 30] [--warmup 10] [--ordering original|rcm]
 //              [--min-sample-ms 0] [--tpr-csv FILE] [--csv FILE] [--precision all|fp64|fp32|fp16]
+//              [--accumulate wide|half]
 //
 // Per matrix and precision: every layout (i32, i16, i8, r16, r8, lp) at every threads per row T; every
 // result checked against CSR-i32 of the same precision at the same T (it must be bit-identical, so
@@ -35,6 +36,8 @@ struct Args {
   std::string tpr_csv;
   std::string ordering = "original";
   std::string precision = "all";
+  // "half": FP16 values summed in FP16, FP16 only (the reference's bench_csr_width_fp16acc build)
+  std::string accumulate = "wide";
   int reps = 30;
   int warmup = 10;
   double min_sample_ms = 0.0;
@@ -256,6 +259,7 @@ void run_precision(spmv_csr* matrix, const std::string& name, int dtype, const A
   for (int tpr : kThreadsPerRow) {
     spmv_operator_config config;
     spmv_operator_config_init(&config, SPMV_LAYOUT_I32, dtype, tpr);
+    if (args.accumulate == "half") config.accumulate = SPMV_ACCUMULATE_HALF;
     spmv_operator* op = nullptr;
     check(spmv_operator_create(matrix, &config, &op), "operator");
     check(spmv_operator_run(op, v.x, v.y, stream), "run");
@@ -295,6 +299,7 @@ void run_precision(spmv_csr* matrix, const std::string& name, int dtype, const A
       if (!admissible) continue;
       spmv_operator_config config;
       spmv_operator_config_init(&config, layout.code, dtype, tpr);
+      if (args.accumulate == "half") config.accumulate = SPMV_ACCUMULATE_HALF;
       spmv_operator* op = nullptr;
       check(spmv_operator_create(matrix, &config, &op), "operator");
       spmv_memory memory;
@@ -379,7 +384,7 @@ Args parse(int argc, char** argv) {
     if (option == "--help" || i + 1 >= argc) {
       std::printf("usage: spmv_bench --matrix A.mtx [--matrix B.mtx ...] [--reps 30] [--warmup 10] "
                   "[--ordering original|rcm] [--min-sample-ms 0] [--tpr-csv FILE] [--csv FILE] "
-                  "[--precision all|fp64|fp32|fp16]\n");
+                  "[--precision all|fp64|fp32|fp16] [--accumulate wide|half]\n");
       std::exit(option == "--help" ? 0 : 1);
     }
     const std::string value = argv[++i];
@@ -391,12 +396,14 @@ Args parse(int argc, char** argv) {
     else if (option == "--min-sample-ms") args.min_sample_ms = std::stod(value);
     else if (option == "--tpr-csv") args.tpr_csv = value;
     else if (option == "--precision") args.precision = value;
+    else if (option == "--accumulate") args.accumulate = value;
     else die("unknown option " + option);
   }
   if (args.matrices.empty()) die("at least one --matrix is required");
   if (args.ordering != "original" && args.ordering != "rcm") die("--ordering must be original or rcm");
   if (args.precision != "all" && args.precision != "fp64" && args.precision != "fp32" && args.precision != "fp16")
     die("--precision must be all, fp64, fp32 or fp16");
+  if (args.accumulate != "wide" && args.accumulate != "half") die("--accumulate must be wide or half");
   return args;
 }
 
@@ -444,7 +451,8 @@ int main(int argc, char** argv) {
     std::printf("  %-4s %-10s %-3s %-4s %8s %8s %8s %8s %5s %6s %6s %9s\n", "prec", "row ptr", "col", "tpr", "t[ms]",
                 "GFLOP/s", "GB/s", "", "eps", "pred", "meas", "max|dy|");
     for (int dtype : {SPMV_F64, SPMV_F32, SPMV_F16})
-      if (args.precision == "all" || args.precision == precision_name(dtype))
+      if ((args.precision == "all" || args.precision == precision_name(dtype)) &&
+          (args.accumulate == "wide" || dtype == SPMV_F16))   // FP16 sums: the FP16 products only
         run_precision(matrix, name, dtype, args, read_bandwidth, sparse, stream);
     spmv_csr_destroy(matrix);
   }

@@ -40,6 +40,8 @@ NUMPY_DTYPES = {F64: np.float64, F32: np.float32, F16: np.float16}
 VALUE_BYTES = {F64: 8, F32: 4, F16: 2}
 THREADS_PER_ROW = (2, 4, 8, 16, 32)
 SCHEDULE_AUTO, SCHEDULE_TILES, SCHEDULE_CLASSES = 0, 1, 2
+# the type FP16 values are summed in (SPMV_ACCUMULATE_*): FP32, or FP16 (the half-accumulate control build)
+ACCUMULATE_WIDE, ACCUMULATE_HALF = 0, 1
 
 OK = 0
 ERR_INVALID_ARGUMENT, ERR_IO, ERR_FORMAT, ERR_NOT_ADMISSIBLE, ERR_OUT_OF_MEMORY = 1, 2, 3, 4, 5
@@ -91,7 +93,7 @@ class OperatorConfig(ctypes.Structure):
     _fields_ = [("layout", ctypes.c_int), ("dtype", ctypes.c_int), ("tpr", ctypes.c_int),
                 ("physical_tpr", ctypes.c_int), ("tile_nnz", ctypes.c_int), ("value_rounding", ctypes.c_int),
                 ("device", ctypes.c_int), ("stages", ctypes.c_int), ("tile_rows", ctypes.c_int),
-                ("schedule", ctypes.c_int)]
+                ("schedule", ctypes.c_int), ("accumulate", ctypes.c_int)]
 
 
 class OperatorInfo(ctypes.Structure):
@@ -527,7 +529,7 @@ class Operator:
 
     def __init__(self, matrix: CsrMatrix, layout: int, dtype: int, tpr: int, physical_tpr: int = 0,
                  tile_nnz: int = 0, value_rounding: int = 0, device: int = -1, stages: int = 0, tile_rows: int = 0,
-                 schedule: int = 0):
+                 schedule: int = 0, accumulate: int = 0):
         config = OperatorConfig()
         _lib.spmv_operator_config_init(ctypes.byref(config), layout, dtype, tpr)
         config.physical_tpr = physical_tpr
@@ -537,6 +539,7 @@ class Operator:
         config.stages = stages
         config.tile_rows = tile_rows
         config.schedule = schedule
+        config.accumulate = accumulate
         handle = ctypes.c_void_p()
         _check(_lib.spmv_operator_create(matrix.handle, ctypes.byref(config), ctypes.byref(handle)))
         self._handle = handle

@@ -40,7 +40,7 @@ def test_help_and_argument_errors():
     done = subprocess.run([binary, "--help"], capture_output=True, text=True, timeout=60)
     assert done.returncode == 0 and done.stdout.startswith("usage: spmv_bench --matrix A.mtx")
     for arguments in (["--bogus", "1"], [], ["--matrix", "a.mtx", "--ordering", "amd"],
-                      ["--matrix", "a.mtx", "--precision", "bf16"]):
+                      ["--matrix", "a.mtx", "--precision", "bf16"], ["--matrix", "a.mtx", "--accumulate", "fp8"]):
         assert subprocess.run([binary] + arguments, capture_output=True, timeout=60).returncode == 1
 
 
@@ -91,3 +91,22 @@ def test_campaign_rows_on_smoke_matrices(smoke_matrix_paths, tmp_path):
     for row in library:
         assert row["status"] == "ok", row
         assert float(row["max_rel_diff"]) <= CUSPARSE_TOLERANCE[row["prec"]], row
+
+
+@pytest.mark.gpu
+def test_half_sums_campaign_rows(smoke_matrix_paths, tmp_path):
+    """--accumulate half (the reference's bench_csr_width_fp16acc): FP16 rows only, every layout still
+    bit-identical to CSR-i32 at the same T (all of them sum in FP16 in the same order)."""
+    binary = built()
+    results = tmp_path / "results.csv"
+    name, path = sorted(smoke_matrix_paths.items())[0]
+    local = tmp_path / os.path.basename(path)
+    os.symlink(path, local)
+    done = subprocess.run([binary, "--matrix", str(local), "--reps", "2", "--warmup", "1", "--accumulate", "half",
+                           "--csv", str(results)], capture_output=True, text=True, timeout=900)
+    assert done.returncode == 0, done.stdout[-2000:] + done.stderr[-2000:]
+    rows = [r for r in csv.DictReader(open(results)) if r["kernel"] == "custom"]
+    assert len(rows) == 6 and all(r["prec"] == "fp16" for r in rows)
+    for row in rows:
+        if row["status"] == "ok":
+            assert float(row["max_abs_diff"]) == 0.0, row
