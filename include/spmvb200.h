@@ -180,10 +180,11 @@ int spmv_encode_lane_packed_device(const int* row_ptr, const int* col_ind, int r
  * front under a fixed budget, loops that cannot stall on cudaMalloc/cudaFree. No counterpart in the
  * reference (its encoder runs on the host). Limits: rows at most 2^26 (SPMV_ERR_TOO_LARGE above); the
  * scratch is a fixed 512 KiB array inside the library, held on every GPU that loads it until the process
- * exits. The first call on a device looks up that array's address on the device (make that first call
- * before any stream capture). All calls share the array, so calls that overlap on the GPU (other streams,
- * other host threads) race on it; nothing in it needs clearing between calls. Same arguments, results
- * and two-call use as spmv_encode_lane_packed_device. */
+ * exits. The first call on a device, and the first after that device's context was reset
+ * (cudaDeviceReset), looks up that array's address on the device (make that first call before any stream
+ * capture). All calls share the array, so calls that overlap on the GPU (other streams, other host
+ * threads) race on it; nothing in it needs clearing between calls. Synchronises the stream. Same
+ * arguments, results and two-call use as spmv_encode_lane_packed_device. */
 int spmv_encode_lane_packed_device_noalloc(const int* row_ptr, const int* col_ind, int rows, int tpr, int* row_word,
                                            uint8_t* row_width, uint32_t* words, int64_t word_capacity,
                                            int64_t* word_count, void* stream);
@@ -363,8 +364,9 @@ int spmv_chain_run(const spmv_operator* shard_op, spmv_comm* comm, const int* sh
  * places in the next x; the round of blocks c * nranks .. c * nranks + nranks - 1 is all-gathered in
  * place on a stream of the communicator's own while block c + 1 computes, and the products leave a few
  * multiprocessors to those collectives. Results are those of spmv_chain_run; x_current, x_next, the
- * parity of products and the stream mean the same. No counterpart in the reference (its benchmark is
- * single-GPU). */
+ * parity of products and the stream mean the same; after an error both x buffers are undefined (the
+ * call returns only once the collectives it queued have finished). No counterpart in the reference (its
+ * benchmark is single-GPU). */
 int spmv_chain_run_blocks(const spmv_operator* const* block_ops, int blocks_per_rank, int block_rows,
                           spmv_comm* comm, void* x_current, void* x_next, int products, void* stream);
 

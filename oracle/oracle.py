@@ -26,11 +26,13 @@ F16_HALF_SUMS = 3
 NUMPY = {F64: np.float64, F32: np.float32, F16: np.float16, F16_HALF_SUMS: np.float16}
 
 
-def build(reference: bool = False):
-    """Builds liboracle.so (and, with reference=True, the _ref checkers from the reference sources)."""
+def build(reference: bool = False, reference_root: str = ""):
+    """Builds liboracle.so (and, with reference=True, the _ref checkers from the reference sources under
+    reference_root, or under SPMV_REFERENCE_ROOT when that is empty)."""
     subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
     if reference:
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+        extra = [f"REFERENCE_ROOT={reference_root}"] if reference_root else []
+        subprocess.run(["make", "-s", "-C", HERE, "ref"] + extra, check=True)
 
 
 def _load_oracle():
@@ -60,6 +62,8 @@ def _load_oracle():
     lib.oracle_convert_values.restype = None
     lib.oracle_convert_values.argtypes = [i, i64, v, v]
     lib.oracle_max_threads.restype = i
+    lib.oracle_set_threads.restype = None
+    lib.oracle_set_threads.argtypes = [i]
     lib.oracle_tpr_slot.restype = i
     lib.oracle_tpr_slot.argtypes = [i]
     return lib
@@ -76,6 +80,12 @@ def _p(array: Optional[np.ndarray]):
 
 def max_threads() -> int:
     return _oracle.oracle_max_threads()
+
+
+def set_threads(count: int) -> None:
+    """Sets the threads the oracle's products use by default. A launcher such as torch.distributed.run
+    exports OMP_NUM_THREADS=1, which would otherwise hold the oracle to one core."""
+    _oracle.oracle_set_threads(int(count))
 
 
 # ---- encoders (bench_csr_width.cu:149-285, 795-917) --------------------------------------------------------

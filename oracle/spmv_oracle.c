@@ -436,6 +436,15 @@ int oracle_spmv(int dtype, int layout, int tpr, int rows, const int* row_ptr, co
   return 0;
 }
 
+/* Sets the number of threads the oracle SpMV uses by default (count >= 1). */
+void oracle_set_threads(int count) {
+#ifdef _OPENMP
+  if (count >= 1) omp_set_num_threads(count);
+#else
+  (void)count;
+#endif
+}
+
 /* Number of threads the oracle SpMV uses by default (the host cores OpenMP sees). */
 int oracle_max_threads(void) {
 #ifdef _OPENMP

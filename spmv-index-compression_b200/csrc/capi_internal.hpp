@@ -18,6 +18,15 @@ int guarded(const std::function<void()>& body);
 void require(bool condition, const char* message);
 // The caller's facts, or facts_of(matrix) when facts is null.
 Facts facts_for(const spmv_csr* matrix, const spmv_facts* facts);
+// Makes `device` current (when it is >= 0 and not already) and restores the caller's device when it goes
+// out of scope.
+struct DeviceScope {
+  int previous = -1;
+  explicit DeviceScope(int device);
+  ~DeviceScope();
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+};
 // One product on `stream` whose tile kernel launches free_sms multiprocessors' worth of persistent CTAs
 // fewer, so that kernels running beside it (collectives) find free multiprocessors (operator.cu).
 cudaError_t run_operator_leaving_sms(const spmv_operator* op, const void* x, void* y, cudaStream_t stream, int free_sms);

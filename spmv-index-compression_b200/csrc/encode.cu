@@ -7,11 +7,13 @@
 //   2. a scan of the words per row into row_word (block scans, a scan of the block sums, an add);
 //   3. k_lp_pack     one warp per row: every delta OR-ed into its words at bit
 //                    width * (lane * quotient + min(lane, remainder) + step), lane-major.
+#include <cuda.h>   // CUcontext and CUresult (types only: the driver calls come through the runtime's entry points)
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "capi_internal.hpp"
 
@@ -278,20 +280,51 @@ __global__ void k_scan_add_in_place(const long long* __restrict__ sums, int64_t 
   if (index < count) row_word[index] = (int)(row_word[index] + sums[index / kScanBlock]);
 }
 
-// The address of g_encode_scratch on each device, taken once per device with that device current.
+// The unique ID of the context current on this thread (0 when none is): the driver's cuCtxGetCurrent and
+// cuCtxGetId, reached through the runtime's driver entry points, so the library does not link libcuda.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static const std::pair<GetCurrent, GetId> driver = [] {
+    void* current = nullptr;
+    void* id = nullptr;
+    cudaDriverEntryPointQueryResult found_current = cudaDriverEntryPointSymbolNotFound, found_id = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &current, cudaEnableDefault, &found_current) != cudaSuccess ||
+        found_current != cudaDriverEntryPointSuccess)
+      current = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &id, cudaEnableDefault, &found_id) != cudaSuccess ||
+        found_id != cudaDriverEntryPointSuccess)
+      id = nullptr;
+    return std::make_pair(reinterpret_cast<GetCurrent>(current), reinterpret_cast<GetId>(id));
+  }();
+  CUcontext context = nullptr;
+  unsigned long long id = 0;
+  if (!driver.first || !driver.second || driver.first(&context) != CUDA_SUCCESS || !context ||
+      driver.second(context, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// The address of g_encode_scratch on the current device, taken with that device current: once per device,
+// and again when the device's context is not the one the address was taken in (cudaDeviceReset, or a
+// framework that tears the primary context down, gives the device a new context and the array a new
+// address).
 long long* encode_scratch_address() {
   static std::mutex guard;
   static long long* address[64] = {};
+  static unsigned long long context[64] = {};
   int device = 0;
   const cudaError_t status = cudaGetDevice(&device);
   if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(status));
   if (device < 0 || device >= 64) fail(SPMV_ERR_UNSUPPORTED, "device ordinal above 63");
   std::lock_guard<std::mutex> lock(guard);
-  if (!address[device]) {
+  const unsigned long long id = current_context_id();
+  if (!address[device] || id == 0 || id != context[device]) {
     void* pointer = nullptr;
-    const cudaError_t found = cudaGetSymbolAddress(&pointer, g_encode_scratch);
+    const cudaError_t found = cudaGetSymbolAddress(&pointer, g_encode_scratch);   // makes the context current
     if (found != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(found));
     address[device] = static_cast<long long*>(pointer);
+    context[device] = current_context_id();
   }
   return address[device];
 }

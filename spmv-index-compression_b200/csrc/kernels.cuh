@@ -345,70 +345,6 @@ __device__ __forceinline__ Acc reduce_lanes(Acc (&acc)[T / P]) {
   return sum;
 }
 
-// ---- the vector path -----------------------------------------------------------------------------------
-// One group of T threads per row, each thread one logical lane, straight from global memory. CTA `block`
-// of `blocks` (of BLOCK threads each) takes the rows item = group, group + groups, ... of the row list.
-template <class V, int LAYOUT, int T, int BLOCK>
-__device__ __forceinline__ void vector_rows(const KernelArgs& a, int64_t block, int64_t blocks) {
-  using VT = ValueTraits<V>;
-  using Acc = typename VT::Acc;
-  using Index = typename LayoutTraits<LAYOUT>::Index;
-  constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
-  constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
-  const V* values = static_cast<const V*>(a.values);
-  const V* x = static_cast<const V*>(a.x);
-  V* y = static_cast<V*>(a.y);
-  const int lane = threadIdx.x & (T - 1);
-  const int64_t group = (block * BLOCK + threadIdx.x) / T;
-  const int64_t groups = (blocks * BLOCK) / T;
-
-  for (int64_t first = 0; first < a.row_count; first += groups) {   // the same trip count on every thread
-    const int64_t item = first + group;
-    const int row = item < a.row_count ? (a.row_list ? a.row_list[item] : (int)item) : 0;
-    Acc sum = Acc(0);
-    if (item < a.row_count) {
-      const int64_t entry_begin = a.row_ptr[row], entry_end = a.row_ptr[row + 1];
-      if constexpr (!kPacked) {
-        const Index* columns = static_cast<const Index*>(a.columns);
-        const int base = kBase ? a.row_base[row] : 0;
-#pragma unroll 4
-        for (int64_t entry = entry_begin + lane; entry < entry_end; entry += T)
-          sum = VT::fma(VT::widen(load_readonly(values + entry)),
-                        VT::widen(load_readonly(x + base + (int)load_readonly(columns + entry))), sum);
-      } else {
-        // the reference's decode (bench_csr_width.cu:482-510): a 64-bit window over the lane's run
-        const int length = (int)(entry_end - entry_begin);
-        const int quotient = length / T, remainder = length - quotient * T;
-        const int mine = quotient + (lane < remainder ? 1 : 0);
-        const int width = a.row_width[row];
-        const uint64_t mask = width == 0 ? 0ull : (~0ull >> (64 - width));
-        const int64_t start_bit = (int64_t)width * ((int64_t)lane * quotient + (lane < remainder ? lane : remainder));
-        const int64_t word = (int64_t)a.row_word[row] + (start_bit >> 5);
-        uint64_t window = (((uint64_t)load_readonly(a.words + word + 1) << 32) | load_readonly(a.words + word)) >> (start_bit & 31);
-        int available = 64 - (int)(start_bit & 31);
-        int64_t next_word = word + 2;
-        int column = a.row_base[row];
-        int64_t entry = entry_begin + lane;
-        for (int taken = 0; taken < mine; ++taken) {
-          column += (int)(window & mask);
-          sum = VT::fma(VT::widen(load_readonly(values + entry)), VT::widen(load_readonly(x + column)), sum);
-          window >>= width;
-          available -= width;
-          entry += T;
-          if (available < width) {
-            window |= (uint64_t)load_readonly(a.words + next_word) << available;
-            available += 32;
-            ++next_word;
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int offset = T / 2; offset > 0; offset >>= 1) sum = VT::add(sum, __shfl_down_sync(0xffffffffu, sum, offset, T));
-    if (lane == 0 && item < a.row_count) y[row] = VT::narrow(sum);
-  }
-}
-
 // ---- rows on groups of P threads ----------------------------------------------------------------------
 // Where a row's data is read from: the shifted images of a resident tile in shared memory, or the
 // operator's arrays in global memory (read-only path). Both are indexed by absolute row, entry and word.
@@ -471,10 +407,66 @@ struct GlobalView {
 // Delta of a CSR-lp lane at bit `bit` of the row's stream starting at word w0 (bit width * (lane *
 // quotient + min(lane, remainder) + k) for its k-th delta, lane_major_bit of the reference): the two
 // 32-bit words around it always hold it (a width never exceeds 32 bits).
-template <class View>
-__device__ __forceinline__ uint32_t packed_delta(const View& view, int64_t w0, uint32_t bit, uint32_t mask) {
-  const int64_t w = w0 + (bit >> 5);
-  return __funnelshift_r(view.word(w), view.word(w + 1), bit & 31) & mask;
+template <class View, class Bit>
+__device__ __forceinline__ uint32_t packed_delta(const View& view, int64_t w0, Bit bit, uint32_t mask) {
+  const int64_t w = w0 + (int64_t)(bit >> 5);
+  return __funnelshift_r(view.word(w), view.word(w + 1), (uint32_t)(bit & 31)) & mask;
+}
+
+// ---- the vector path -----------------------------------------------------------------------------------
+// One group of T threads per row, each thread one logical lane, straight from global memory. CTA `block`
+// of `blocks` (of BLOCK threads each) takes the rows item = group, group + groups, ... of the row list.
+template <class V, int LAYOUT, int T, int BLOCK>
+__device__ __forceinline__ void vector_rows(const KernelArgs& a, int64_t block, int64_t blocks) {
+  using VT = ValueTraits<V>;
+  using Acc = typename VT::Acc;
+  using Index = typename LayoutTraits<LAYOUT>::Index;
+  constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
+  constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
+  const V* values = static_cast<const V*>(a.values);
+  const V* x = static_cast<const V*>(a.x);
+  V* y = static_cast<V*>(a.y);
+  const int lane = threadIdx.x & (T - 1);
+  const int64_t group = (block * BLOCK + threadIdx.x) / T;
+  const int64_t groups = (blocks * BLOCK) / T;
+
+  for (int64_t first = 0; first < a.row_count; first += groups) {   // the same trip count on every thread
+    const int64_t item = first + group;
+    const int row = item < a.row_count ? (a.row_list ? a.row_list[item] : (int)item) : 0;
+    Acc sum = Acc(0);
+    if (item < a.row_count) {
+      const int64_t entry_begin = a.row_ptr[row], entry_end = a.row_ptr[row + 1];
+      if constexpr (!kPacked) {
+        const Index* columns = static_cast<const Index*>(a.columns);
+        const int base = kBase ? a.row_base[row] : 0;
+#pragma unroll 4
+        for (int64_t entry = entry_begin + lane; entry < entry_end; entry += T)
+          sum = VT::fma(VT::widen(load_readonly(values + entry)),
+                        VT::widen(load_readonly(x + base + (int)load_readonly(columns + entry))), sum);
+      } else {
+        // logical lane `lane` owns the row's deltas lane * quotient + min(lane, remainder) + k, k < its count
+        // (lane-major order); each is a funnel shift of the two words around its bit offset, which may pass
+        // 2^32 bits in a long row
+        const GlobalView<V, LAYOUT> view(a);
+        const int64_t length = entry_end - entry_begin;
+        const int64_t quotient = length / T, remainder = length - quotient * T;
+        const int64_t count = quotient + (lane < remainder ? 1 : 0);
+        const uint32_t width = view.row_width(row);
+        const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
+        const int64_t w0 = view.row_word(row);
+        uint64_t bit = (uint64_t)width * (uint64_t)(lane * quotient + (lane < remainder ? lane : remainder));
+        int column = view.row_base(row);
+        int64_t entry = entry_begin + lane;
+        for (int64_t k = 0; k < count; ++k, entry += T, bit += width) {
+          column += (int)packed_delta(view, w0, bit, mask);
+          sum = VT::fma(VT::widen(load_readonly(values + entry)), VT::widen(load_readonly(x + column)), sum);
+        }
+      }
+    }
+#pragma unroll
+    for (int offset = T / 2; offset > 0; offset >>= 1) sum = VT::add(sum, __shfl_down_sync(0xffffffffu, sum, offset, T));
+    if (lane == 0 && item < a.row_count) y[row] = VT::narrow(sum);
+  }
 }
 
 // The product of one row (entries [entry_begin, entry_end), column base `base` for the row-relative and

@@ -228,13 +228,10 @@ int spmv_chain_run_blocks(const spmv_operator* const* block_ops, int blocks_per_
     const size_t value_bytes = (size_t)value_bytes_of(dtype);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     NcclApi& api = nccl();
+    // the side stream and the events live on the communicator's device, whichever device is current
+    DeviceScope scope(comm->device);
     if (!comm->side) {
-      // the side stream lives on the communicator's device, whichever device is current
-      int previous = 0;
-      cudaError_t created = cudaGetDevice(&previous);
-      if (created == cudaSuccess && previous != comm->device) created = cudaSetDevice(comm->device);
-      if (created == cudaSuccess) created = cudaStreamCreateWithFlags(&comm->side, cudaStreamNonBlocking);
-      if (previous != comm->device) cudaSetDevice(previous);
+      const cudaError_t created = cudaStreamCreateWithFlags(&comm->side, cudaStreamNonBlocking);
       if (created != cudaSuccess) {
         comm->side = nullptr;
         fail(SPMV_ERR_CUDA, std::string("side stream: ") + cudaGetErrorString(created));
@@ -275,7 +272,12 @@ int spmv_chain_run_blocks(const spmv_operator* const* block_ops, int blocks_per_
       if (status == cudaSuccess) status = cudaStreamWaitEvent(s, gathered, 0);
       std::swap(current, next);
     }
-    if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("chained products over row blocks: ") + cudaGetErrorString(status));
+    if (status != cudaSuccess) {
+      // all-gathers already queued on the side stream may still write x_next: let them finish before the
+      // call returns its error (x_next is undefined after an error)
+      cudaStreamSynchronize(comm->side);
+      fail(SPMV_ERR_CUDA, std::string("chained products over row blocks: ") + cudaGetErrorString(status));
+    }
   });
 }
 

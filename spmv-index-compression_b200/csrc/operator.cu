@@ -32,18 +32,6 @@ void cuda_check(cudaError_t status, const char* what) {
   fail(code, std::string(what) + ": " + cudaGetErrorString(status));
 }
 
-// Restores the caller's current device when it goes out of scope.
-struct DeviceScope {
-  int previous = -1;
-  explicit DeviceScope(int device) {
-    cuda_check(cudaGetDevice(&previous), "cudaGetDevice");
-    if (device >= 0 && device != previous) cuda_check(cudaSetDevice(device), "cudaSetDevice");
-  }
-  ~DeviceScope() {
-    if (previous >= 0) cudaSetDevice(previous);
-  }
-};
-
 // A device copy of count elements followed by kStreamPadding zero bytes, so that a tile's bulk copy may
 // round its end up to the next 16-byte boundary.
 template <class T>
@@ -80,6 +68,14 @@ struct DeviceBuffer {
 constexpr int64_t kDeviceEncodeNnz = 1 << 20;
 
 }  // namespace
+
+DeviceScope::DeviceScope(int device) {
+  cuda_check(cudaGetDevice(&previous), "cudaGetDevice");
+  if (device >= 0 && device != previous) cuda_check(cudaSetDevice(device), "cudaSetDevice");
+}
+DeviceScope::~DeviceScope() {
+  if (previous >= 0) cudaSetDevice(previous);
+}
 
 // encode.cu
 int64_t device_lane_packed_layout(const int* row_ptr, const int* col_ind, int rows, int tpr, int* row_word,
@@ -725,8 +721,13 @@ int spmv_operator_run_host_batch(const spmv_operator* op, const void* x_host, in
       if (status == cudaSuccess) status = cudaEventRecord(copied_out[b], copy_out);
     }
     if (status == cudaSuccess && count > 0) status = cudaStreamWaitEvent(copy_in, copied_out[(count - 1) & 1], 0);
-    if (status == cudaSuccess) status = cudaStreamSynchronize(copy_in);
-    if (status == cudaSuccess) status = cudaStreamSynchronize(copy_out);
+    // every stream drains before the call returns, after an error too: no copy into the caller's buffers
+    // may still run once it has returned (the first error is the one reported)
+    for (cudaStream_t drained : {copy_in, compute, copy_out}) {
+      if (!drained) continue;
+      const cudaError_t synchronized = cudaStreamSynchronize(drained);
+      if (status == cudaSuccess) status = synchronized;
+    }
     for (int b = 0; b < 2; ++b)
       for (cudaEvent_t event : {copied_in[b], computed[b], copied_out[b]})
         if (event) cudaEventDestroy(event);

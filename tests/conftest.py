@@ -16,7 +16,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, os.path.join(ROOT, "spmv-index-compression_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
-REFERENCE_ROOT = os.environ.get("SPMV_REFERENCE_ROOT", "/root/reference")
+# the reference tree, when the environment names one (SPMV_REFERENCE_ROOT); tests that need it skip otherwise
+REFERENCE_ROOT = os.environ.get("SPMV_REFERENCE_ROOT", "")
 DATA = os.path.join(ROOT, "tests", "_data")
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
@@ -26,8 +27,10 @@ def pytest_configure(config):
 
 
 def smoke_matrix_archive(name):
-    for candidate in (os.path.join(DATA, name + ".mtx.gz"),
-                      os.path.join(REFERENCE_ROOT, "data", "smoke_matrices", name + ".mtx.gz")):
+    candidates = [os.path.join(DATA, name + ".mtx.gz")]
+    if REFERENCE_ROOT:
+        candidates.append(os.path.join(REFERENCE_ROOT, "data", "smoke_matrices", name + ".mtx.gz"))
+    for candidate in candidates:
         if os.path.exists(candidate):
             return candidate
     return None

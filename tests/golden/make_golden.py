@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Regenerates the golden fixtures of tests/golden/ from the reference (HERMES-TorVerLab/spmv-index-compression).
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference tree>   (or SPMV_REFERENCE_ROOT set)
 
 Reads the reference tree as text and data, and runs the reference's own code compiled from its sources
 (oracle/_ref, `make -C oracle ref`). Writes:
@@ -139,10 +139,12 @@ def reference_streams(ref):
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default=os.environ.get("SPMV_REFERENCE_ROOT", "/root/reference"))
+    parser.add_argument("--reference", default=os.environ.get("SPMV_REFERENCE_ROOT", ""))
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("name the reference tree with --reference or SPMV_REFERENCE_ROOT")
     import oracle
-    oracle.build(reference=True)
+    oracle.build(reference=True, reference_root=args.reference)
     ref = oracle.Reference()
     published_rows(args.reference)
     characterization_rows(args.reference)

@@ -16,16 +16,16 @@ pytestmark = pytest.mark.gpu
 def encode(build, matrix, tpr):
     row_ptr, col_ind, _ = matrix.arrays()
     device_row_ptr = torch.from_numpy(row_ptr.astype(np.int32)).cuda()
-    device_col = torch.from_numpy(col_ind.astype(np.int32)).cuda()
-    row_word = torch.full((matrix.rows,), -7, dtype=torch.int32, device="cuda")
-    row_width = torch.full((matrix.rows,), 99, dtype=torch.uint8, device="cuda")
+    device_col = torch.from_numpy(col_ind.astype(np.int32) if col_ind.size else np.zeros(1, np.int32)).cuda()
+    row_word = torch.full((max(matrix.rows, 1),), -7, dtype=torch.int32, device="cuda")
+    row_width = torch.full((max(matrix.rows, 1),), 99, dtype=torch.uint8, device="cuda")
     count = build(device_row_ptr.data_ptr(), device_col.data_ptr(), matrix.rows, tpr, row_word.data_ptr(),
                   row_width.data_ptr())
     words = torch.full((count,), -1, dtype=torch.int32, device="cuda")
     assert build(device_row_ptr.data_ptr(), device_col.data_ptr(), matrix.rows, tpr, row_word.data_ptr(),
                  row_width.data_ptr(), words.data_ptr(), count) == count
     torch.cuda.synchronize()
-    return row_word.cpu().numpy(), row_width.cpu().numpy(), words.cpu().numpy()
+    return row_word.cpu().numpy()[:matrix.rows], row_width.cpu().numpy()[:matrix.rows], words.cpu().numpy()
 
 
 def test_two_calls_in_a_row_match_the_allocating_encoder():
@@ -34,6 +34,20 @@ def test_two_calls_in_a_row_match_the_allocating_encoder():
     second = spmv.CsrMatrix.from_arrays(70000, 9000, *random_csr(70000, 9000, 6.0, 32, empty_every=101))
     for tpr in (2, 8, 32):
         for matrix in (first, second, first):
+            mine = encode(spmv.build_packed_deltas_device_noalloc, matrix, tpr)
+            theirs = encode(spmv.build_packed_deltas_device, matrix, tpr)
+            for a, b in zip(mine, theirs):
+                assert np.array_equal(a, b), (tpr, matrix.rows)
+
+
+def test_edge_matrices_match_the_allocating_encoder():
+    """Deltas of 31 bits, a matrix with no rows, and 1.1 M short rows: 1075 scan blocks, so the sums of the
+    blocks are scanned across more than one chunk of 1024."""
+    wide = spmv.CsrMatrix.from_arrays(3, (1 << 31) - 1, [0, 3, 3, 5], [0, 1 << 30, (1 << 31) - 2, 5, 7])
+    empty = spmv.CsrMatrix.from_arrays(0, 10, [0], [], [])
+    many = spmv.synth_random_band(1_100_000, 40, 3.0, 9)
+    for tpr in (2, 32):
+        for matrix in (wide, empty, many, wide):
             mine = encode(spmv.build_packed_deltas_device_noalloc, matrix, tpr)
             theirs = encode(spmv.build_packed_deltas_device, matrix, tpr)
             for a, b in zip(mine, theirs):
