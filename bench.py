@@ -2,7 +2,7 @@
 """bench.py — CSR SpMV with compressed column indices on B200: GFLOP/s (2·nnz/t) and effective HBM GB/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload stencil27]
-                    [--layout lp] [--tpr 8] [--no-sweep]
+                    [--layout lp] [--tpr 8] [--no-sweep] [--no-chained]
 
 A step is one product y = A x over the whole matrix (at N GPUs: every rank its nnz-balanced row shard,
 x replicated, no exchange — the products are independent). The default workload is the 3D 27-point
@@ -11,12 +11,19 @@ then RCM-permuted; FP64; x uniform [-1, 1] from seed 2; the headline layout is C
 not admissible there: after RCM a row spans up to 151,688 columns). The working set (1.2-1.4 GB) is ten
 times the 126 MB L2, so no flush is needed between products.
 
-Prints ONE JSON line on rank 0. `value` is device-timed whole-job GFLOP/s (CUDA events, barrier and
-synchronize on both sides, max over ranks); `e2e` is the same metric through the public API from pinned
-host memory (x copied in and y copied out every step); `roofline` relates the kernel's algorithmic bytes
-(the reference byte model, memory_of) per launch to the measured HBM peak; `cpu_baseline` is the
-reference-order CSR-i32 product on the host cores (the CPU oracle, a restatement of the reference kernel).
-`--impl reference` times that CPU implementation alone on the same workload and metric.
+Prints ONE JSON line on rank 0. `value` is device-timed whole-job GFLOP/s over exactly K back-to-back
+products (CUDA events on the launching stream, barrier and synchronize on both sides, max over ranks);
+`protocol` adds the same product timed with the reference's protocol (3 warm-ups, 20 samples of at least
+10 ms, median). `e2e` is the same metric through the public API from pinned host memory: x copied in and y
+copied out every step (at N GPUs each rank copies its 1/N slice of x and the slices are all-gathered over
+NCCL). `roofline` relates the kernel's algorithmic bytes (the reference byte model, memory_of) per launch
+to the measured HBM peak. `parity` is the headline y compared bit for bit with the CPU oracle's
+reference-order CSR-i32 product at the same T (each rank its rows). `chained` is the block-FEM matrix
+(n = 32M, 2.05 G nonzeros, FP32) row-sharded over the N GPUs, K chained products y -> x whose all-gather
+runs inside the product over NVLink peer memory. At N = 1, `per_layout` sweeps every layout and T on the
+stencil, the random band and the power-law matrix, `comparators` times cuSPARSE and the reference's own
+kernels rebuilt for sm_100a on the same arrays, and `cpu_baseline` is the reference-order CSR-i32 product on
+the host cores. `--impl reference` times that CPU implementation alone on the same workload and metric.
 """
 import argparse
 import json
@@ -38,13 +45,16 @@ WORKLOADS = {
     "band": "random band n=1M, half-bandwidth 2000, Poisson(32)+diagonal, FP32, seed 1",
     "powerlaw": "power law n=8M, Zipf(1.8) row lengths in [1,100000] rescaled to mean 12, FP16, seed 3",
     "fem": "block FEM n=32M, 8x8 blocks, diagonal + 7 block-columns at offsets U[-50000,50000], FP32, seed 4; "
-           "chained products y -> x with an NCCL all-gather of y",
+           "chained products y -> x, the all-gather of y inside the product over NVLink peer memory",
 }
 DTYPE_OF = {"stencil27": "fp64", "laplacian": "fp64", "band": "fp32", "powerlaw": "fp16", "fem": "fp32"}
 SEED_OF = {"stencil27": 2, "laplacian": 0, "band": 1, "powerlaw": 3, "fem": 4}
 FEM_ROWS = 32_000_000
 METRIC = "SpMV GFLOP/s & HBM GB/s (vs ~8 TB/s) per layout/T at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
+SWEEP_TPR = {"stencil27": (8, 32), "band": (2, 4, 8, 16, 32), "powerlaw": (32,)}
+SWEEP_LAYOUTS = {"stencil27": ("i32", "i16", "r16", "lp"), "band": ("i32", "i16", "r16", "lp"),
+                 "powerlaw": ("i32", "i16", "r16", "lp")}
 
 
 def parse_args():
@@ -53,17 +63,17 @@ def parse_args():
     parser.add_argument("--steps", type=int, default=2000)
     parser.add_argument("--warmup", type=int, default=20)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="stencil27")
+    parser.add_argument("--workload", choices=("stencil27", "laplacian", "band", "powerlaw"), default="stencil27")
     parser.add_argument("--layout", default="lp")
     parser.add_argument("--tpr", type=int, default=8)
     parser.add_argument("--physical-tpr", type=int, default=0)
     parser.add_argument("--tile-nnz", type=int, default=0)
     parser.add_argument("--fem-rows", type=int, default=FEM_ROWS,
-                        help="fem: n of the block-FEM matrix (a multiple of 8; smaller n for profiling captures)")
-    parser.add_argument("--blocks-per-rank", type=int, default=0,
-                        help="fem: interleaved row blocks per rank whose all-gathers overlap the next block's "
-                             "product (0: 4 on more than one GPU, else 1; 1: one shard and spmv_chain_run)")
+                        help="chained: n of the block-FEM matrix (a multiple of 8; smaller n for quick runs)")
+    parser.add_argument("--chain-layouts", default="i32,lp", help="chained: layouts, comma-separated")
+    parser.add_argument("--chain-tpr", type=int, default=8)
     parser.add_argument("--no-sweep", action="store_true", help="skip the per-layout/T table and comparators")
+    parser.add_argument("--no-chained", action="store_true", help="skip the chained block-FEM products")
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget")
     return parser.parse_args()
 
@@ -112,6 +122,11 @@ def profiled_traffic(workload, layout, tpr):
         if len(fields) >= 4 and not line.startswith("#") and fields[:3] == [workload, layout, str(tpr)]:
             return float(fields[3])
     return None
+
+
+def host_cores():
+    """The host threads this process may run on (its affinity mask)."""
+    return len(os.sched_getaffinity(0))
 
 
 class ClockSampler:
@@ -169,29 +184,41 @@ class ClockSampler:
                 "power_w_max": max(power) if power else None, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def sampler_for(torch, local_rank):
+    gpu_id = str(torch.cuda.get_device_properties(local_rank).uuid)
+    return ClockSampler(gpu_id if gpu_id.startswith("GPU-") else f"GPU-{gpu_id}")
+
+
 # ---------------------------------------------------------------------------------------------------------
-# the reference arm: the reference-order CPU product (the oracle)
+# the oracle's legs: the CPU baseline, the reference arm, and the checker of the products (never timed,
+# never the product: the oracle restates the reference's CSR-i32 kernel order on the host)
 # ---------------------------------------------------------------------------------------------------------
-def cpu_product_rate(matrix, dtype_code, tpr, seconds_budget, steps=None, warmup=0):
-    """Times the CPU oracle's CSR-i32 product on all host threads. With steps, times exactly that many
-    samples after warmup, each a row block sized so the whole run fits the budget; otherwise as many full
-    products as fit in the budget. Returns (GFLOP/s, description, cores)."""
+def oracle_module(threads):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
+    oracle.set_threads(max(1, threads))   # a launcher's OMP_NUM_THREADS=1 would hold it to one core
+    return oracle
+
+
+def cpu_product_rate(matrix, dtype_code, tpr, seconds_budget, steps=None, warmup=0):
+    """Times the CPU oracle's CSR-i32 product on every host thread of this process. With steps, times
+    exactly that many samples after warmup, each a row block sized so the whole run fits the budget;
+    otherwise as many full products as fit in the budget. Returns (GFLOP/s, description, cores)."""
     import spmvb200 as spmv
+    cores = host_cores()
+    oracle = oracle_module(cores)
     row_ptr, col_ind, values = matrix.arrays()
     x = spmv.fill_uniform(dtype_code, matrix.cols, 7)
     typed = oracle.convert_values(values, dtype_code)
-    cores = oracle.max_threads()
     start = time.perf_counter()
-    oracle.spmv(dtype_code, oracle.I32, tpr, row_ptr, typed, x, columns=col_ind)
+    oracle.spmv(dtype_code, oracle.I32, tpr, row_ptr, typed, x, columns=col_ind, threads=cores)
     full = time.perf_counter() - start
     nnz = col_ind.size
     if steps is None:
         count = max(1, int(seconds_budget / max(full, 1e-6)))
         start = time.perf_counter()
         for _ in range(count):
-            oracle.spmv(dtype_code, oracle.I32, tpr, row_ptr, typed, x, columns=col_ind)
+            oracle.spmv(dtype_code, oracle.I32, tpr, row_ptr, typed, x, columns=col_ind, threads=cores)
         elapsed = time.perf_counter() - start
         return 2.0 * nnz * count / elapsed / 1e9, f"{count} full products of the workload", cores
     fraction = min(1.0, seconds_budget / max((steps + warmup) * full, 1e-9))
@@ -199,23 +226,33 @@ def cpu_product_rate(matrix, dtype_code, tpr, seconds_budget, steps=None, warmup
     sample_ptr = row_ptr[:rows + 1]
     sample_nnz = int(sample_ptr[-1])
     for _ in range(warmup):
-        oracle.spmv(dtype_code, oracle.I32, tpr, sample_ptr, typed, x, columns=col_ind)
+        oracle.spmv(dtype_code, oracle.I32, tpr, sample_ptr, typed, x, columns=col_ind, threads=cores)
     start = time.perf_counter()
     for _ in range(steps):
-        oracle.spmv(dtype_code, oracle.I32, tpr, sample_ptr, typed, x, columns=col_ind)
+        oracle.spmv(dtype_code, oracle.I32, tpr, sample_ptr, typed, x, columns=col_ind, threads=cores)
     elapsed = time.perf_counter() - start
     return (2.0 * sample_nnz * steps / elapsed / 1e9,
             f"rows [0, {rows}) of the workload ({sample_nnz} nonzeros, {100 * fraction:.2f}%) per step", cores)
+
+
+def oracle_mismatches(row_ptr, col_ind, values, x, y, dtype_code, tpr, threads):
+    """Rows of y that differ in any bit from the oracle's reference-order CSR-i32 product at T, and the
+    largest absolute difference."""
+    oracle = oracle_module(threads)
+    want = oracle.spmv_csr(row_ptr, col_ind, values, x, dtype_code, oracle.I32, tpr, threads=threads)
+    got = np.ascontiguousarray(y)
+    differ = got.view(np.uint8).reshape(got.size, -1) != want.view(np.uint8).reshape(want.size, -1)
+    rows = int(np.count_nonzero(differ.any(axis=1)))
+    delta = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    delta = delta[np.isfinite(delta)]   # rows of inf or NaN are counted as mismatched by their bits alone
+    return rows, float(delta.max()) if delta.size else 0.0
 
 
 def run_reference(args, rank, world):
     import spmvb200 as spmv
     if rank != 0:
         return
-    if args.workload == "fem":   # a row range of the 2.05 G-nonzero matrix stands in (host memory)
-        matrix = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, 0, min(FEM_ROWS, 2_000_000))
-    else:
-        matrix = build_matrix(spmv, args.workload)
+    matrix = build_matrix(spmv, args.workload)
     dtype_code = spmv.DTYPE_BY_NAME[DTYPE_OF[args.workload]]
     budget = 120.0
     rate, sample, cores = cpu_product_rate(matrix, dtype_code, args.tpr, budget, steps=args.steps, warmup=args.warmup)
@@ -224,7 +261,7 @@ def run_reference(args, rank, world):
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": DTYPE_OF[args.workload], "data": "synthetic",
         "config": {"workload": WORKLOADS[args.workload], "layout": "i32", "tpr": args.tpr, "rows": matrix.rows,
-                   "nnz": matrix.nnz, "parallelism": "host threads (OpenMP over rows)"},
+                   "nnz": matrix.nnz, "parallelism": f"host threads (OpenMP over rows), {cores} cores"},
         "cpu_baseline": {"value": round(rate, 3), "unit": "GFLOP/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(rate, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -234,7 +271,7 @@ def run_reference(args, rank, world):
 
 
 # ---------------------------------------------------------------------------------------------------------
-# our arm
+# timing
 # ---------------------------------------------------------------------------------------------------------
 def event_ms(torch, stream, body, repeats):
     start = torch.cuda.Event(enable_timing=True)
@@ -264,10 +301,43 @@ def protocol_median_ms(torch, stream, body, samples=20, warmup=3, min_sample_ms=
     return statistics.median(times), batch
 
 
+class Ranks:
+    """The job's process group (None on one GPU): barriers and reductions over the ranks."""
+
+    def __init__(self, torch, dist, local_rank):
+        self.torch, self.dist, self.local_rank = torch, dist, local_rank
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier(device_ids=[self.local_rank])
+        self.torch.cuda.synchronize()
+
+    def max(self, values):
+        if self.dist is None:
+            return list(values)
+        tensor = self.torch.tensor(list(values), dtype=self.torch.float64, device=f"cuda:{self.local_rank}")
+        self.dist.all_reduce(tensor, op=self.dist.ReduceOp.MAX)
+        return tensor.tolist()
+
+    def sum(self, values):
+        if self.dist is None:
+            return list(values)
+        tensor = self.torch.tensor(list(values), dtype=self.torch.float64, device=f"cuda:{self.local_rank}")
+        self.dist.all_reduce(tensor, op=self.dist.ReduceOp.SUM)
+        return tensor.tolist()
+
+    def gather_objects(self, item, world):
+        if self.dist is None:
+            return [item]
+        out = [None] * world
+        self.dist.all_gather_object(out, item)
+        return out
+
+
+# ---------------------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------------------
 def run_ours(args, rank, world, local_rank):
-    if args.workload == "fem":
-        run_fem(args, rank, world, local_rank)
-        return
     import torch
     import spmvb200 as spmv
     dist = None
@@ -276,18 +346,21 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(device)
+    ranks = Ranks(torch, dist, local_rank)
     dtype_name = DTYPE_OF[args.workload]
     dtype_code = spmv.DTYPE_BY_NAME[dtype_name]
     torch_dtype = {"fp64": torch.float64, "fp32": torch.float32, "fp16": torch.float16}[dtype_name]
     layout = spmv.LAYOUT_BY_NAME[args.layout]
+    value_bytes = spmv.VALUE_BYTES[dtype_code]
+    threads = max(1, host_cores() // world)
 
     matrix = build_matrix(spmv, args.workload)
     total_nnz, rows, cols = matrix.nnz, matrix.rows, matrix.cols
     bounds = spmv.shard_rows(matrix, world)
-    shard = matrix if world == 1 else matrix.slice_rows(int(bounds[rank]), int(bounds[rank + 1]))
+    first, last = int(bounds[rank]), int(bounds[rank + 1])
+    shard = matrix if world == 1 else matrix.slice_rows(first, last)
     facts = spmv.facts_of(shard)
-    admissible = spmv.configuration_admissible(shard, facts, spmv.Configuration.of(layout, dtype_code, args.tpr))
-    if not admissible:
+    if not spmv.configuration_admissible(shard, facts, spmv.Configuration.of(layout, dtype_code, args.tpr)):
         raise SystemExit(f"layout {args.layout} at T={args.tpr} is not admissible for {args.workload}")
     op = spmv.Operator(shard, layout, dtype_code, args.tpr, physical_tpr=args.physical_tpr, tile_nnz=args.tile_nnz,
                        device=local_rank)
@@ -298,71 +371,92 @@ def run_ours(args, rank, world, local_rank):
     y = torch.empty(shard.rows, dtype=torch_dtype, device=device)
     launch = lambda: op.run(x.data_ptr(), y.data_ptr(), stream.cuda_stream)  # noqa: E731
 
-    def barrier():
-        if dist is not None:
-            dist.barrier(device_ids=[local_rank])
-        torch.cuda.synchronize()
-
     # warm-up, then exactly K timed products bracketed by barrier + synchronize
     for _ in range(args.warmup):
         launch()
-    barrier()
-    gpu_id = torch.cuda.get_device_properties(local_rank).uuid
-    sampler = ClockSampler(f"GPU-{gpu_id}" if not str(gpu_id).startswith("GPU-") else str(gpu_id))
+    ranks.barrier()
+    sampler = sampler_for(torch, local_rank)
     sampler.start()
-    barrier()
+    ranks.barrier()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for _ in range(args.steps):
         launch()
     end.record(stream)
-    barrier()
+    ranks.barrier()
     clocks = sampler.stop()
     elapsed_ms = start.elapsed_time(end)
     op.check()
-    if dist is not None:
-        timing = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(timing, op=dist.ReduceOp.MAX)
-        elapsed_ms = timing.item()
+    (elapsed_ms,) = ranks.max([elapsed_ms])
     ms_per_step = elapsed_ms / args.steps
     value = 2.0 * total_nnz * args.steps / (elapsed_ms * 1e-3) / 1e9
     # the kernel is the only launch of a step: its average duration is the device time per step
     achieved_gbs = algorithmic_bytes / (ms_per_step * 1e-3) / 1e9
 
-    # end to end through the public API from pinned host buffers: copy x in, multiply, copy y out, wait
-    value_bytes = spmv.VALUE_BYTES[dtype_code]
+    # the same product under the reference's protocol (3 warm-ups, 20 samples of at least 10 ms)
+    protocol_ms, protocol_batch = protocol_median_ms(torch, stream, launch)
+    (protocol_ms,) = ranks.max([protocol_ms])
+
+    # parity: this rank's rows of y against the oracle's reference-order CSR-i32 product at the same T
+    launch()
+    torch.cuda.synchronize()
+    y_host = y.cpu().numpy()
+    s_ptr, s_col, s_val = shard.arrays()
+    mismatched, max_abs = oracle_mismatches(s_ptr, s_col, s_val, x_host, y_host, dtype_code, args.tpr, threads)
+    mismatched_total, = ranks.sum([mismatched])
+    (max_abs,) = ranks.max([max_abs])
+    parity = {"checked": True, "against": f"oracle reference-order CSR-i32 product at T={args.tpr} (oracle/spmv_oracle.c)",
+              "rows": rows, "mismatched_rows": int(mismatched_total), "max_abs_diff": max_abs,
+              "bit_identical": mismatched_total == 0}
+
+    # end to end through the public API from pinned host buffers: every step copies its x in (at N GPUs each
+    # rank its 1/N slice, all-gathered over NCCL) and its y out, overlapped with the neighbouring products
     x_pinned = torch.from_numpy(x_host).pin_memory()
     y_pinned = torch.empty(shard.rows, dtype=torch_dtype).pin_memory()
-    # a stream of e2e_steps products through spmv_operator_run_host_batch: every step copies its x in from
-    # pinned host memory and its y out, overlapped with the products of the neighbouring steps
     e2e_steps = max(1, min(args.steps, 200))
     pitch = lambda count: (count * value_bytes + 15) // 16 * 16  # noqa: E731
-    x_pair = torch.empty(2 * pitch(cols), dtype=torch.uint8, device=device)
     y_pair = torch.empty(2 * pitch(shard.rows), dtype=torch.uint8, device=device)
-    batch = lambda steps: op.run_host_batch(x_pinned.data_ptr(), 0, y_pinned.data_ptr(), 0, steps,  # noqa: E731
-                                            x_pair.data_ptr(), y_pair.data_ptr(), stream.cuda_stream)
+    comm = None
+    if world == 1:
+        x_pair = torch.empty(2 * pitch(cols), dtype=torch.uint8, device=device)
+        batch = lambda steps: op.run_host_batch(x_pinned.data_ptr(), 0, y_pinned.data_ptr(), 0, steps,  # noqa: E731
+                                                x_pair.data_ptr(), y_pair.data_ptr(), stream.cuda_stream)
+    else:
+        box = ranks.gather_objects(spmv.comm_unique_id() if rank == 0 else None, world)
+        comm = spmv.Comm(world, rank, box[0], device=local_rank)
+        slice_count = (cols + world - 1) // world
+        x_pair = torch.empty(2 * pitch(slice_count * world), dtype=torch.uint8, device=device)
+        batch = lambda steps: spmv.shard_run_host_batch(op, comm, x_pinned.data_ptr(), 0, y_pinned.data_ptr(), 0,  # noqa: E731
+                                                        steps, x_pair.data_ptr(), y_pair.data_ptr(), stream.cuda_stream)
     batch(3)
-    barrier()
+    ranks.barrier()
     # the given stream waits for the last copy out, so its events bracket the whole batch
     e2e_ms = event_ms(torch, stream, lambda: batch(e2e_steps), 1)
-    barrier()
-    if dist is not None:
-        timing = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(timing, op=dist.ReduceOp.MAX)
-        e2e_ms = timing.item()
+    ranks.barrier()
+    (e2e_ms,) = ranks.max([e2e_ms])
     e2e_value = 2.0 * total_nnz * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    if comm is not None:
+        comm.check(stream.cuda_stream, 60000)
+        comm.close()
+    e2e_y_ok = bool(np.array_equal(y_pinned.numpy().view(np.uint8), y_host.view(np.uint8)))
 
     extras = {}
+    chained = None
+    if not args.no_chained:
+        del x, y
+        op.close()
+        chained = chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threads)
     if world == 1 and not args.no_sweep:
-        extras = sweep(args, torch, spmv, matrix, dtype_code, torch_dtype, x, stream)
+        extras = sweep(args, torch, spmv, matrix, dtype_code, torch_dtype, stream)
         rate, sample, cores = cpu_product_rate(matrix, dtype_code, args.tpr, args.cpu_seconds)
         extras["cpu_baseline"] = {"value": round(rate, 3), "unit": "GFLOP/s", "cores": cores, "kind": "port",
                                   "sample": sample + " (reference-order CSR-i32, oracle/spmv_oracle.c)"}
     if rank != 0:
         return
     peak, peak_source = measured_peak()
-    traffic = profiled_traffic(args.workload, args.layout, args.tpr)
+    # the committed ncu capture is of the whole matrix on one GPU; a shard's traffic was not captured
+    traffic = profiled_traffic(args.workload, args.layout, args.tpr) if world == 1 else None
     # x gathers: one per nonzero; against the measured rate of random single-element gathers from an
     # array the size of x (the ceiling for scattered columns, where each element costs a 32-byte sector)
     gather_ceiling = spmv.gather_rate(cols, value_bytes, 10)
@@ -374,218 +468,247 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": WORKLOADS[args.workload], "layout": args.layout, "tpr": args.tpr,
                    "physical_tpr": info.physical_tpr, "tile_nnz": info.tile_nnz, "rows": rows, "cols": cols,
                    "nnz": total_nnz, "parallelism": f"row shards x{world} (nnz-balanced, x replicated)",
-                   "l2": f"no flush: working set {algorithmic_bytes * world / 1e9:.2f} GB > 126 MB L2",
+                   "l2": f"no flush: working set {algorithmic_bytes / 1e9:.2f} GB per rank > 126 MB L2",
                    "schedule": "classes" if info.schedule == spmv.SCHEDULE_CLASSES else "tiles",
                    "tiles": info.tiles, "listed_rows": info.listed_rows, "long_rows": info.long_rows},
+        "protocol": {"value": f"{args.steps} back-to-back products between CUDA events after {args.warmup} warm-ups",
+                     "reference_protocol_ms": round(protocol_ms, 6), "reference_protocol_batch": protocol_batch,
+                     "reference_protocol_gflops": round(2.0 * total_nnz / (protocol_ms * 1e-3) / 1e9, 3),
+                     "reference_protocol": "3 warm-ups, 20 samples of back-to-back products lasting >= 10 ms, "
+                                           "median (bench_csr_width.cu:631-663)"},
+        "parity": parity,
         "effective_gbs": round(achieved_gbs * world, 1),
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved_gbs / peak, 4), "traffic": traffic, "peak_source": peak_source,
                      "kernel": "k_spmv_classes" if info.schedule == spmv.SCHEDULE_CLASSES else "k_spmv_tiles",
-                     "algorithmic_bytes_per_launch": algorithmic_bytes},
+                     "algorithmic_bytes_per_launch": algorithmic_bytes,
+                     "traffic_note": None if world == 1 else "per-shard DRAM traffic not captured"},
         "x_gathers": {"per_step": total_nnz, "achieved_per_s": round(gather_rate, 1),
                       "random_gather_ceiling_per_s": round(gather_ceiling, 1),
                       "frac": round(gather_rate / gather_ceiling, 4),
                       "note": "ceiling measured by spmv_gather_rate on an array of cols elements; above 1 means the "
                               "gathers reuse L1/L2 lines"},
         "clocks": clocks,
-        "e2e": {"value": round(e2e_value, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": cols * value_bytes * world,
-                "d2h_bytes_per_step": rows * value_bytes, "steps": e2e_steps},
+        "e2e": {"value": round(e2e_value, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": cols * value_bytes,
+                "d2h_bytes_per_step": rows * value_bytes, "steps": e2e_steps, "y_matches_device_run": e2e_y_ok,
+                "path": "spmv_operator_run_host_batch" if world == 1 else
+                        "spmv_shard_run_host_batch: each rank copies its 1/N slice of x, NCCL all-gather, product, "
+                        "its rows of y out"},
         "gpu_launches": args.steps,
     }
+    if chained is not None:
+        line["chained"] = chained
     line.update(extras)
     print(json.dumps(line), flush=True)
 
 
-def run_fem(args, rank, world, local_rank):
-    """The block-FEM matrix row-sharded over the ranks (each rank builds only its rows), a step is one
-    chained product. On one shard per rank (spmv_chain_run): every rank's shard product into its slice of
-    the next x, then the slices all-gathered over NCCL. On interleaved row blocks (spmv_chain_run_blocks,
-    the default on more than one GPU): rank r holds blocks c * world + r of 32M / (world * C) rows, and each
-    round of blocks is all-gathered while the next block computes. The kernel alone is also timed for the
-    roofline."""
-    import torch
-    import spmvb200 as spmv
-    dist = None
+def chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threads):
+    """Config 5: the block-FEM matrix row-sharded over the ranks (each rank builds only its rows), K chained
+    products y -> x. Each product stores the rank's rows of y into every rank's next x over NVLink peer
+    memory (spmv_chain_run_peer), then a barrier of the GPUs; the product kernels alone are timed too, and
+    one more product is checked on a block of each rank's rows against the oracle."""
+    dtype = spmv.F32
+    tpr = args.chain_tpr
+    bounds = fem_bounds(world)
+    first, last = int(bounds[rank]), int(bounds[rank + 1])
+    started = time.time()
+    shard = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, first, last)
+    facts = spmv.facts_of(shard)
+    x_host = spmv.fill_uniform(dtype, FEM_ROWS, SEED_OF["fem"])
+    group = spmv.PeerGroup(world, rank, x_host.nbytes, device=local_rank)
     if world > 1:
-        import torch.distributed as dist
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    stream = torch.cuda.current_stream(device)
-    dtype_code = spmv.DTYPE_BY_NAME["fp32"]
-    layout = spmv.LAYOUT_BY_NAME[args.layout]
-    blocks_per_rank = args.blocks_per_rank or (4 if world > 1 else 1)
-    total_nnz = 64 * FEM_ROWS
-    if blocks_per_rank == 1:
-        bounds = fem_bounds(world)
-        ranges = [(int(bounds[rank]), int(bounds[rank + 1]))]
-    else:
-        block_rows = FEM_ROWS // (world * blocks_per_rank)
-        if block_rows * world * blocks_per_rank != FEM_ROWS or block_rows % 8:
-            raise SystemExit(f"{FEM_ROWS} rows do not divide into {world * blocks_per_rank} blocks of whole 8x8 blocks")
-        ranges = [((c * world + rank) * block_rows, (c * world + rank + 1) * block_rows) for c in range(blocks_per_rank)]
-    ops = []
-    for first, last in ranges:
-        shard = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, first, last)
-        facts = spmv.facts_of(shard)
-        if not spmv.configuration_admissible(shard, facts, spmv.Configuration.of(layout, dtype_code, args.tpr)):
-            raise SystemExit(f"layout {args.layout} at T={args.tpr} is not admissible for fem")
-        ops.append(spmv.Operator(shard, layout, dtype_code, args.tpr, physical_tpr=args.physical_tpr,
-                                 tile_nnz=args.tile_nnz, device=local_rank))
-        del shard
-    info = ops[0].info()
-    algorithmic_bytes = sum(op.info().memory.total for op in ops)
-    box = [spmv.comm_unique_id() if rank == 0 else None]
-    if dist is not None:
-        dist.broadcast_object_list(box, src=0)
-    comm = spmv.Comm(world, rank, box[0], device=local_rank)
-    x_host = spmv.fill_uniform(dtype_code, FEM_ROWS, SEED_OF["fem"])
-    x_current = torch.from_numpy(x_host).to(device)
-    x_next = torch.zeros_like(x_current)
-    y_alone = torch.empty(max(last - first for first, last in ranges), dtype=torch.float32, device=device)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier(device_ids=[local_rank])
-        torch.cuda.synchronize()
-
-    if blocks_per_rank == 1:
-        chain = lambda count: spmv.chain_run(ops[0], comm, bounds, x_current.data_ptr(), x_next.data_ptr(),  # noqa: E731
-                                             count, stream.cuda_stream)
-    else:
-        chain = lambda count: spmv.chain_run_blocks(ops, block_rows, comm, x_current.data_ptr(),  # noqa: E731
-                                                    x_next.data_ptr(), count, stream.cuda_stream)
-    chain(args.warmup)
-    comm.check(stream.cuda_stream, 120000)
-    barrier()
-    gpu_id = torch.cuda.get_device_properties(local_rank).uuid
-    sampler = ClockSampler(f"GPU-{gpu_id}" if not str(gpu_id).startswith("GPU-") else str(gpu_id))
-    sampler.start()
-    barrier()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    chain(args.steps)
-    end.record(stream)
-    comm.check(stream.cuda_stream, 120000)
-    barrier()
-    clocks = sampler.stop()
-    elapsed_ms = start.elapsed_time(end)
-
-    # the product kernels alone on this rank's rows (x held still), for the roofline
-    def products_alone():
-        for op in ops:
-            op.run(x_current.data_ptr(), y_alone.data_ptr(), stream.cuda_stream)
-    kernel_steps = max(3, min(args.steps, 50))
-    kernel_ms = event_ms(torch, stream, products_alone, kernel_steps)
-    for op in ops:
-        op.check()
-    # end to end: x in from pinned host memory, one chained product, this rank's new rows of x out
-    x_pinned = torch.from_numpy(x_host).pin_memory()
-    own_rows = sum(last - first for first, last in ranges)
-    y_pinned = torch.empty(own_rows, dtype=torch.float32).pin_memory()
-    e2e_steps = max(1, min(args.steps, 10))
-
-    def e2e_step():
-        x_current.copy_(x_pinned, non_blocking=True)
-        chain(1)
-        offset = 0
-        for first, last in ranges:
-            y_pinned[offset:offset + last - first].copy_(x_next[first:last], non_blocking=True)
-            offset += last - first
-    barrier()
-    e2e_ms = event_ms(torch, stream, e2e_step, e2e_steps)
-    comm.check(stream.cuda_stream, 120000)
-    barrier()
-    times = torch.tensor([elapsed_ms, kernel_ms, e2e_ms], dtype=torch.float64, device=device)
-    if dist is not None:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    elapsed_ms, kernel_ms, e2e_ms = times.tolist()
-    comm.close()
-    if rank != 0:
-        return
-    ms_per_step = elapsed_ms / args.steps
-    kernel_ms_per_launch = kernel_ms / kernel_steps
-    achieved_gbs = algorithmic_bytes / (kernel_ms_per_launch * 1e-3) / 1e9
-    peak, peak_source = measured_peak()
-    if blocks_per_rank == 1:
-        parallelism = (f"row shards x{world} (block-aligned, nnz-balanced), NCCL all-gather of y between chained "
-                       "products")
-    else:
-        parallelism = (f"interleaved row blocks x{world * blocks_per_rank} ({blocks_per_rank} per rank, "
-                       f"{block_rows} rows each), each round's NCCL all-gather beside the next block's product")
-    line = {
-        "metric": METRIC, "value": round(2.0 * total_nnz * args.steps / (elapsed_ms * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": WORKLOADS["fem"].replace("n=32M", f"n={FEM_ROWS}") if FEM_ROWS != 32_000_000
-                   else WORKLOADS["fem"], "layout": args.layout, "tpr": args.tpr, "rows": FEM_ROWS,
-                   "nnz": total_nnz, "parallelism": parallelism,
-                   "l2": f"no flush: {algorithmic_bytes / 1e9:.2f} GB per rank > 126 MB L2",
-                   "physical_tpr": info.physical_tpr, "tile_nnz": info.tile_nnz,
-                   "tiles": sum(op.info().tiles for op in ops)},
-        "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved_gbs / peak, 4), "traffic": None, "peak_source": peak_source,
-                     "kernel": "k_spmv_tiles", "algorithmic_bytes_per_launch": algorithmic_bytes // len(ops),
-                     "kernel_ms": round(kernel_ms_per_launch / len(ops), 6)},
-        "clocks": clocks,
-        "e2e": {"value": round(2.0 * total_nnz * e2e_steps / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GFLOP/s",
-                "h2d_bytes_per_step": FEM_ROWS * 4 * world, "d2h_bytes_per_step": FEM_ROWS * 4, "steps": e2e_steps},
-        "gpu_launches": args.steps * len(ops),
-    }
-    for op in ops:
-        op.close()
-    print(json.dumps(line), flush=True)
-
-
-def sweep(args, torch, spmv, matrix, dtype_code, torch_dtype, x, stream):
-    """Every layout at T = 8 and 32 with the reference's timing protocol, and cuSPARSE on the same matrix."""
+        group.open(ranks.gather_objects(group.export(), world))
     peak, _ = measured_peak()
-    facts = spmv.facts_of(matrix)
-    rows = []
-    i32_ms = {}
-    y = torch.empty(matrix.rows, dtype=torch_dtype, device=x.device)
-    for tpr in (8, 32):
-        for name in ("i32", "i16", "r16", "lp"):
-            layout = spmv.LAYOUT_BY_NAME[name]
-            configuration = spmv.Configuration.of(layout, dtype_code, tpr)
-            memory = spmv.memory_of(matrix, facts, configuration)
-            entry = {"layout": name, "tpr": tpr, "bytes": memory.total}
-            if not spmv.configuration_admissible(matrix, facts, configuration):
-                entry["status"] = "not admissible"
-                rows.append(entry)
-                continue
-            with spmv.Operator(matrix, layout, dtype_code, tpr) as op:
-                ms, batch = protocol_median_ms(torch, stream, lambda: op.run(x.data_ptr(), y.data_ptr(), stream.cuda_stream))
-                entry.update(status="ok", physical_tpr=op.info().physical_tpr, tile_nnz=op.info().tile_nnz,
-                             schedule="classes" if op.info().schedule == spmv.SCHEDULE_CLASSES else "tiles",
-                             t_ms=round(ms, 6), batch=batch,
-                             gflops=round(2.0 * matrix.nnz / (ms * 1e-3) / 1e9, 2),
-                             gbs=round(memory.total / (ms * 1e-3) / 1e9, 1),
-                             frac=round(memory.total / (ms * 1e-3) / 1e9 / peak, 4))
-            if name == "i32":
-                i32_ms[tpr] = ms
-            entry["speedup_vs_i32"] = round(i32_ms[tpr] / entry["t_ms"], 4) if tpr in i32_ms else None
-            rows.append(entry)
+    total_nnz = 64 * FEM_ROWS
+    sample_rows = min(65536, last - first)
+    sample = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, first, first + sample_rows)
+    s_ptr, s_col, s_val = sample.arrays()
+    # the first rows of the next rank's shard, which reach this rank only through the peers' stores
+    peer_first = int(bounds[(rank + 1) % world])
+    peer_rows = min(65536, int(bounds[(rank + 1) % world + 1]) - peer_first)
+    peer_sample = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, peer_first, peer_first + peer_rows)
+    p_ptr, p_col, p_val = peer_sample.arrays()
+    out = {"workload": WORKLOADS["fem"].replace("n=32M", f"n={FEM_ROWS}"), "rows": FEM_ROWS, "nnz": total_nnz,
+           "tpr": tpr, "steps": args.steps, "warmup": args.warmup, "n_gpus": world,
+           "parallelism": f"row shards x{world} (block-aligned, equal nonzeros); every product stores its rows into "
+                          "every rank's next x over NVLink peer memory, then a barrier of the GPUs",
+           "layouts": {}}
+    y_alone = torch.empty(last - first, dtype=torch.float32, device=f"cuda:{local_rank}")
+    for name in [item for item in args.chain_layouts.split(",") if item]:
+        layout = spmv.LAYOUT_BY_NAME[name]
+        if not spmv.configuration_admissible(shard, facts, spmv.Configuration.of(layout, dtype, tpr)):
+            out["layouts"][name] = {"status": "not admissible"}
+            continue
+        op = spmv.Operator(shard, layout, dtype, tpr, device=local_rank)
+        info = op.info()
+        # one chained product from x0, its rows checked against the oracle on a block of this rank's rows and
+        # on the first rows of the next rank's shard (rows that reached this rank through its peers' stores);
+        # checked on the first product because the matrix is diagonally dominant: x grows by about 64 each
+        # product and overflows FP32 within the timed products
+        group.write_x(x_host.ctypes.data, x_host.nbytes)
+        ranks.barrier()
+        spmv.chain_run_peer(op, group, bounds, 1, stream.cuda_stream, timeout_ms=60000)
+        group.check()
+        x_after = np.empty_like(x_host)
+        group.read_x(x_after.ctypes.data, x_after.nbytes)
+        mismatched, max_abs = oracle_mismatches(s_ptr, s_col, s_val, x_host, x_after[first:first + sample_rows],
+                                                dtype, tpr, threads)
+        if world > 1:
+            peer_first = int(bounds[(rank + 1) % world])
+            mismatched_peer, max_peer = oracle_mismatches(p_ptr, p_col, p_val, x_host,
+                                                          x_after[peer_first:peer_first + peer_rows], dtype, tpr,
+                                                          threads)
+            mismatched += mismatched_peer
+            max_abs = max(max_abs, max_peer)
+        ranks.barrier()
+        spmv.chain_run_peer(op, group, bounds, args.warmup, stream.cuda_stream, timeout_ms=60000)
+        group.check()
+        ranks.barrier()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        spmv.chain_run_peer(op, group, bounds, args.steps, stream.cuda_stream, timeout_ms=60000)
+        end.record(stream)
+        end.synchronize()
+        group.check()
+        chain_ms = start.elapsed_time(end)
+        ranks.barrier()
+        # the product kernels alone on this rank's rows, x held still (no stores to peers, no barrier)
+        x_now = group.x(0)
+        kernel_ms = event_ms(torch, stream, lambda: op.run(x_now, y_alone.data_ptr(), stream.cuda_stream),
+                             args.steps) / args.steps
+        op.check()
+        chain_ms, kernel_ms, max_abs = ranks.max([chain_ms, kernel_ms, max_abs])
+        (mismatched,) = ranks.sum([mismatched])
+        ms_per_step = chain_ms / args.steps
+        bytes_per_rank = info.memory.total
+        out["layouts"][name] = {
+            "status": "ok", "ms_per_step": round(ms_per_step, 6),
+            "gflops": round(2.0 * total_nnz / (ms_per_step * 1e-3) / 1e9, 3),
+            "kernel_ms": round(kernel_ms, 6), "exposed_exchange_ms": round(ms_per_step - kernel_ms, 6),
+            "kernel_gbs_per_rank": round(bytes_per_rank / (kernel_ms * 1e-3) / 1e9, 1),
+            "kernel_frac_per_rank": round(bytes_per_rank / (kernel_ms * 1e-3) / 1e9 / peak, 4),
+            "physical_tpr": info.physical_tpr, "tile_nnz": info.tile_nnz,
+            "gpu_launches_per_step": 2,
+            "parity": {"checked": True, "rows_per_rank": sample_rows + (peer_rows if world > 1 else 0),
+                       "mismatched_rows": int(mismatched), "max_abs_diff": max_abs, "bit_identical": mismatched == 0,
+                       "against": f"oracle reference-order CSR-i32 product at T={tpr} of x0, on the first chained "
+                                  "product: a block of each rank's own rows and, at N > 1, of the next rank's rows "
+                                  "as they arrived through peer memory"}}
+        op.close()
+    ranks.barrier()
+    group.close()
+    out["setup_s"] = round(time.time() - started, 1)
+    return out
+
+
+def sweep(args, torch, spmv, stencil, dtype_code, torch_dtype, stream):
+    """Every layout and T on the stencil, the random band and the power-law matrix with the reference's
+    timing protocol, each layout's y compared bit for bit with CSR-i32's at the same T; cuSPARSE on each
+    matrix and the reference's own kernels rebuilt for sm_100a on the stencil's arrays."""
+    peak, _ = measured_peak()
+    rows_out = []
     comparators = {}
+    for workload in ("stencil27", "band", "powerlaw"):
+        matrix = stencil if workload == "stencil27" else build_matrix(spmv, workload)
+        dtype = spmv.DTYPE_BY_NAME[DTYPE_OF[workload]]
+        tdtype = {"fp64": torch.float64, "fp32": torch.float32, "fp16": torch.float16}[DTYPE_OF[workload]]
+        bits_type = {"fp64": torch.int64, "fp32": torch.int32, "fp16": torch.int16}[DTYPE_OF[workload]]
+        facts = spmv.facts_of(matrix)
+        x = torch.from_numpy(spmv.fill_uniform(dtype, matrix.cols, SEED_OF[workload])).cuda()
+        y = torch.empty(matrix.rows, dtype=tdtype, device="cuda")
+        for tpr in SWEEP_TPR[workload]:
+            i32_ms, i32_bits = None, None
+            for name in SWEEP_LAYOUTS[workload]:
+                layout = spmv.LAYOUT_BY_NAME[name]
+                configuration = spmv.Configuration.of(layout, dtype, tpr)
+                memory = spmv.memory_of(matrix, facts, configuration)
+                entry = {"matrix": workload, "layout": name, "tpr": tpr, "bytes": memory.total}
+                if not spmv.configuration_admissible(matrix, facts, configuration):
+                    entry["status"] = "not admissible"
+                    rows_out.append(entry)
+                    continue
+                with spmv.Operator(matrix, layout, dtype, tpr) as op:
+                    body = lambda: op.run(x.data_ptr(), y.data_ptr(), stream.cuda_stream)  # noqa: E731
+                    ms, batch = protocol_median_ms(torch, stream, body)
+                    body()
+                    torch.cuda.synchronize()
+                    op.check()
+                    info = op.info()
+                    if workload == "stencil27" and name in ("i32", "lp"):
+                        comparators.setdefault("reference_sm100a", []).append(
+                            reference_kernels(torch, spmv, op, matrix, dtype, layout, tpr, x, y, ms))
+                bits = y.view(bits_type).clone()
+                if name == "i32":
+                    i32_ms, i32_bits = ms, bits
+                gbs = memory.total / (ms * 1e-3) / 1e9
+                entry.update(status="ok", physical_tpr=info.physical_tpr, tile_nnz=info.tile_nnz,
+                             schedule="classes" if info.schedule == spmv.SCHEDULE_CLASSES else "tiles",
+                             t_ms=round(ms, 6), batch=batch, gflops=round(2.0 * matrix.nnz / (ms * 1e-3) / 1e9, 2),
+                             gbs=round(gbs, 1), frac=round(gbs / peak, 4),
+                             speedup_vs_i32=round(i32_ms / ms, 4) if i32_ms else None,
+                             bits_equal_i32=bool(torch.equal(bits, i32_bits)) if i32_bits is not None else None)
+                rows_out.append(entry)
+        comparators.setdefault("cusparse", {})[workload] = cusparse_comparator(torch, spmv, matrix, facts, dtype, tdtype,
+                                                                                x, stream)
+        del x, y
+        if workload != "stencil27":
+            del matrix
+    return {"per_layout": rows_out, "comparators": comparators}
+
+
+def cusparse_comparator(torch, spmv, matrix, facts, dtype, tdtype, x, stream):
     try:
         row_ptr, col_ind, values = matrix.arrays()
         import warnings
         with warnings.catch_warnings():
             warnings.simplefilter("ignore")
-            compute = torch.float32 if torch_dtype == torch.float16 else torch_dtype
+            compute = torch.float32 if tdtype == torch.float16 else tdtype
             a = torch.sparse_csr_tensor(torch.from_numpy(row_ptr), torch.from_numpy(col_ind),
-                                        torch.from_numpy(values).to(torch_dtype).to(compute), size=(matrix.rows, matrix.cols),
+                                        torch.from_numpy(values).to(tdtype).to(compute), size=(matrix.rows, matrix.cols),
                                         device=x.device)
             xc = x.to(compute).unsqueeze(1)
             ms, batch = protocol_median_ms(torch, stream, lambda: torch.sparse.mm(a, xc))
-            i32 = spmv.memory_of(matrix, facts, spmv.Configuration.of(spmv.I32, dtype_code, 8)).total
-            comparators["cusparse"] = {"via": "torch.sparse.mm (cusparseSpMV, int32 CSR)", "t_ms": round(ms, 6),
-                                       "gflops": round(2.0 * matrix.nnz / (ms * 1e-3) / 1e9, 2),
-                                       "gbs": round(i32 / (ms * 1e-3) / 1e9, 1)}
+            i32 = spmv.memory_of(matrix, facts, spmv.Configuration.of(spmv.I32, dtype, 8)).total
+            out = {"via": "torch.sparse.mm (cusparseSpMV, int32 CSR)", "t_ms": round(ms, 6),
+                   "gflops": round(2.0 * matrix.nnz / (ms * 1e-3) / 1e9, 2), "gbs": round(i32 / (ms * 1e-3) / 1e9, 1),
+                   "compute": str(compute).replace("torch.", "")}
             del a
+            return out
     except Exception as failure:  # the comparator is optional
-        comparators["cusparse"] = {"error": str(failure)[:200]}
-    return {"per_layout": rows, "comparators": comparators}
+        return {"error": str(failure)[:200]}
+
+
+def reference_kernels(torch, spmv, op, matrix, dtype, layout, tpr, x, y, library_ms):
+    """The reference's launch<T> (bench_csr_width.cu:607-629) rebuilt for sm_100a from its own sources
+    (oracle/_ref, built where the reference tree was present), timed with the same protocol on the
+    operator's own device arrays, outside the product path; its y compared with the library's."""
+    name = spmv.LAYOUT_NAMES[layout]
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        if not oracle.Reference.available():
+            return {"layout": name, "tpr": tpr, "unavailable": "oracle/_ref/libspmvref.so is not built"}
+        reference = oracle.Reference()
+        arrays = op.arrays()
+        mine = y.clone()
+        theirs = torch.zeros_like(y)
+        call = lambda: reference.launch_async(dtype, layout, tpr, matrix.rows, matrix.cols, matrix.nnz,  # noqa: E731
+                                              arrays.row_ptr, arrays.columns, arrays.row_base, arrays.row_word,
+                                              arrays.row_width, arrays.words, arrays.values, x.data_ptr(),
+                                              theirs.data_ptr())
+        ms, batch = protocol_median_ms(torch, torch.cuda.default_stream(), call)
+        torch.cuda.synchronize()
+        peak, _ = measured_peak()
+        memory = op.info().memory.total
+        return {"layout": name, "tpr": tpr, "t_ms": round(ms, 6), "batch": batch,
+                "gflops": round(2.0 * matrix.nnz / (ms * 1e-3) / 1e9, 2),
+                "frac": round(memory / (ms * 1e-3) / 1e9 / peak, 4),
+                "bits_equal_library": bool(torch.equal(mine.view(torch.int64) if mine.dtype == torch.float64 else mine,
+                                                       theirs.view(torch.int64) if theirs.dtype == torch.float64 else theirs)),
+                "library_t_ms": round(library_ms, 6), "library_speedup": round(ms / library_ms, 4)}
+    except Exception as failure:  # the comparator is optional
+        return {"layout": name, "tpr": tpr, "error": str(failure)[:200]}
 
 
 def main():
@@ -598,7 +721,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
-        cpus = len(os.sched_getaffinity(0))
+        cpus = host_cores()
         os.environ.setdefault("SPMV_HOST_THREADS", str(max(1, cpus // world)))
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -349,6 +349,18 @@ void spmv_comm_destroy(spmv_comm* comm);
  * spmv_comm_destroy aborts it instead of waiting for the other ranks. */
 int spmv_comm_check(spmv_comm* comm, void* stream, int timeout_ms);
 
+/* End-to-end products of a row shard from host memory with x split over the ranks: for each of count
+ * vectors (x_host + i * x_stride bytes, cols entries; y_host + i * y_stride bytes, the shard's rows) every
+ * rank copies its slice of x (ceil(cols / nranks) entries from rank * that) in from host memory, the
+ * slices are all-gathered in place (one ncclAllGather), the shard's product runs, and its rows of y go
+ * out to host memory; vectors overlap as in spmv_operator_run_host_batch. x_device: two buffers of
+ * nranks * ceil(cols / nranks) entries, each rounded up to 16 bytes; y_device: two of the shard's rows,
+ * likewise. Waits for its streams (at most 120 s for the collectives, then SPMV_ERR_TIMEOUT and the
+ * communicator is aborted). All ranks call it with the same count. No counterpart in the reference (its
+ * benchmark runs on one GPU). */
+int spmv_shard_run_host_batch(const spmv_operator* shard_op, spmv_comm* comm, const void* x_host, int64_t x_stride,
+                              void* y_host, int64_t y_stride, int count, void* x_device, void* y_device, void* stream);
+
 /* Chained products y -> x over the row shards: each rank holds the operator of its rows
  * (shard_row_begin[rank] .. shard_row_begin[rank+1]) and the full x. Every product computes the rank's y
  * shard into its slice of the next x, then all-gathers the slices over NCCL, products times. x_current
@@ -369,6 +381,46 @@ int spmv_chain_run(const spmv_operator* shard_op, spmv_comm* comm, const int* sh
  * benchmark is single-GPU). */
 int spmv_chain_run_blocks(const spmv_operator* const* block_ops, int blocks_per_rank, int block_rows,
                           spmv_comm* comm, void* x_current, void* x_next, int products, void* stream);
+
+/* ---- chained products over peer memory (the all-gather inside the product) ---------------------------
+ * No counterpart in the reference (its benchmark runs on one GPU). A peer group is one rank's share of a
+ * job of nranks processes, one GPU each, on one node whose GPUs reach each other's memory (NVLink):
+ * every rank allocates two x buffers and a block of barrier flags in one allocation, exports it
+ * (spmv_peer_group_handle, 64 bytes), the caller gathers every rank's handle in rank order (e.g. an
+ * all-gather over torch.distributed) and every rank maps the others' (spmv_peer_group_open). A chained
+ * product on rank r multiplies its row shard into its rows of the next x and stores those rows into
+ * every other rank's next x as well (stores over NVLink from the product kernel, no collective library),
+ * then waits at a barrier between the ranks' GPUs (flags in peer memory; each wait bounded by
+ * timeout_ms, after which the group's status word records the timeout and spmv_peer_group_check returns
+ * SPMV_ERR_TIMEOUT). Results equal spmv_chain_run's. Every rank must make the same calls in the same
+ * order (products, barriers); destroy a group only once no rank still runs products into it. */
+#define SPMV_PEER_HANDLE_BYTES 64
+typedef struct spmv_peer_group spmv_peer_group;
+/* At most 16 ranks; x_bytes: the bytes of one x (n entries of the operators' value type). The buffers
+ * start zeroed. */
+int spmv_peer_group_create(int nranks, int rank, int64_t x_bytes, int device, spmv_peer_group** out);
+/* This rank's allocation exported for the other ranks: SPMV_PEER_HANDLE_BYTES bytes into handle. */
+int spmv_peer_group_handle(const spmv_peer_group* group, void* handle);
+/* Maps the other ranks' allocations: handles holds nranks handles in rank order (this rank's is skipped). */
+int spmv_peer_group_open(spmv_peer_group* group, const void* handles);
+/* Device pointer of this rank's current x (which = 0: the next product's input, and after a run the
+ * latest result) or of the other buffer (which = 1). Write x0 into the current x before the first run. */
+int spmv_peer_group_x(const spmv_peer_group* group, int which, void** x);
+/* Copies bytes from buffer (host or device memory) into this rank's current x (direction 0), or from the
+ * current x into buffer (direction 1), on the stream, and waits for the copy. */
+int spmv_peer_group_copy_x(spmv_peer_group* group, int direction, void* buffer, int64_t bytes, void* stream);
+/* A barrier of the ranks' GPUs on the stream, each wait at most timeout_ms. Before spmv_peer_group_open it
+ * only waits (no other rank can be told), so it ends in a timeout on more than one rank. */
+int spmv_peer_group_barrier(spmv_peer_group* group, int timeout_ms, void* stream);
+/* Synchronises the device and reads the group's status word: SPMV_ERR_TIMEOUT if a barrier gave up (the
+ * group then refuses further runs; its buffers are undefined). */
+int spmv_peer_group_check(spmv_peer_group* group);
+/* products chained products y -> x over the row shards (shard_row_begin[0..nranks], the rank's operator
+ * holding rows shard_row_begin[rank] .. shard_row_begin[rank+1] of the square matrix): one barrier, then
+ * per product the fused product and a barrier. The current x advances by products. */
+int spmv_chain_run_peer(const spmv_operator* shard_op, spmv_peer_group* group, const int* shard_row_begin, int products,
+                        int timeout_ms, void* stream);
+void spmv_peer_group_destroy(spmv_peer_group* group);
 
 #ifdef __cplusplus
 }

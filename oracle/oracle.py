@@ -248,6 +248,10 @@ class Reference:
         lib.ref_admissible.argtypes = [v, i, i, i]
         lib.ref_launch.restype = i
         lib.ref_launch.argtypes = [i, i, i, i, i, ll, v, v, v, v, v, v, v, v, v]
+        self.has_async = hasattr(lib, "ref_launch_async")
+        if self.has_async:
+            lib.ref_launch_async.restype = i
+            lib.ref_launch_async.argtypes = [i, i, i, i, i, ll, v, v, v, v, v, v, v, v, v]
         self.lib = lib
 
     @staticmethod
@@ -333,6 +337,14 @@ class Reference:
         """The reference kernels on device pointers (integers); returns the cudaError_t."""
         return self.lib.ref_launch(dtype, layout, tpr, rows, cols, nnz, row_ptr, columns, row_base, row_word, row_width,
                                    words, values, x, y)
+
+    def launch_async(self, dtype, layout, tpr, rows, cols, nnz, row_ptr, columns, row_base, row_word, row_width, words,
+                     values, x, y) -> int:
+        """The reference kernels on the default stream without waiting (back-to-back timing); returns the
+        launch's cudaError_t."""
+        call = self.lib.ref_launch_async if self.has_async else self.lib.ref_launch
+        return call(dtype, layout, tpr, rows, cols, nnz, row_ptr, columns, row_base, row_word, row_width, words,
+                    values, x, y)
 
 
 def reference_characterize(matrix_path: str, ordering: str = "original") -> str:

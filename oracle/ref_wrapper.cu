@@ -155,9 +155,9 @@ int ref_admissible(void* handle, int column_bytes, int mode, int fixed_tpr) {
 // --- the reference kernels rebuilt for sm_100a (launch<T>, :607) ------------------------------
 // Device pointers; layout 0 i32, 1 i16, 2 r16, 3 lp, 4 i8, 5 r8; dtype 0 f64, 1 f32, 2 f16.
 // Launches on the default stream like the reference and synchronises. Returns the cudaError_t.
-int ref_launch(int dtype, int layout, int tpr, int rows, int cols, long long nnz, const int* row_ptr,
-               const void* columns, const int* row_base, const int* row_word, const unsigned char* row_width,
-               const unsigned int* words, const void* values, const void* x, void* y) {
+static int ref_launch_impl(int dtype, int layout, int tpr, int rows, int cols, long long nnz, const int* row_ptr,
+                           const void* columns, const int* row_base, const int* row_word, const unsigned char* row_width,
+                           const unsigned int* words, const void* values, const void* x, void* y, int wait) {
   Configuration configuration;
   configuration.column_bytes = layout == 0 ? 4 : ((layout == 1 || layout == 2) ? 2 : (layout == 3 ? 0 : 1));
   configuration.column_mode = (layout == 2 || layout == 5) ? ColumnMode::row_base
@@ -199,8 +199,25 @@ int ref_launch(int dtype, int layout, int tpr, int rows, int cols, long long nnz
     launch<__half>(tpr, configuration, device);
   }
   cudaError_t status = cudaGetLastError();
-  if (status == cudaSuccess) status = cudaDeviceSynchronize();
+  if (status == cudaSuccess && wait) status = cudaDeviceSynchronize();
   return (int)status;
+}
+
+/* launch<T> on the default stream, then a device synchronize; returns the cudaError_t. */
+int ref_launch(int dtype, int layout, int tpr, int rows, int cols, long long nnz, const int* row_ptr,
+               const void* columns, const int* row_base, const int* row_word, const unsigned char* row_width,
+               const unsigned int* words, const void* values, const void* x, void* y) {
+  return ref_launch_impl(dtype, layout, tpr, rows, cols, nnz, row_ptr, columns, row_base, row_word, row_width, words,
+                         values, x, y, 1);
+}
+
+/* launch<T> on the default stream without waiting (for timing back-to-back launches); returns the launch's
+ * cudaError_t. */
+int ref_launch_async(int dtype, int layout, int tpr, int rows, int cols, long long nnz, const int* row_ptr,
+                     const void* columns, const int* row_base, const int* row_word, const unsigned char* row_width,
+                     const unsigned int* words, const void* values, const void* x, void* y) {
+  return ref_launch_impl(dtype, layout, tpr, rows, cols, nnz, row_ptr, columns, row_base, row_word, row_width, words,
+                         values, x, y, 0);
 }
 
 }  // extern "C"

@@ -30,5 +30,9 @@ struct DeviceScope {
 // One product on `stream` whose tile kernel launches free_sms multiprocessors' worth of persistent CTAs
 // fewer, so that kernels running beside it (collectives) find free multiprocessors (operator.cu).
 cudaError_t run_operator_leaving_sms(const spmv_operator* op, const void* x, void* y, cudaStream_t stream, int free_sms);
+// One product on `stream` that also stores every row of y into the peer_count copies of y at peers[] (other
+// GPUs' memory, indexed by the same rows), at most kMaxPeers (operator.cu).
+cudaError_t run_operator_with_peers(const spmv_operator* op, const void* x, void* y, void* const* peers, int peer_count,
+                                    cudaStream_t stream);
 
 }  // namespace spmvb200

@@ -11,6 +11,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <mutex>
@@ -157,6 +158,114 @@ int spmv_comm_check(spmv_comm* comm, void* stream, int timeout_ms) {
       }
       std::this_thread::sleep_for(std::chrono::microseconds(200));
     }
+  });
+}
+
+}  // extern "C"
+
+namespace {
+// Waits until the stream's work is done or a collective failed, for at most timeout_ms; on an NCCL error or
+// the timeout the communicator is marked aborted. Returns SPMV_OK, SPMV_ERR_NCCL, SPMV_ERR_CUDA or
+// SPMV_ERR_TIMEOUT.
+int wait_for_stream(spmv_comm* comm, cudaStream_t s, int timeout_ms) {
+  const auto start = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t async = ncclSuccess;
+    if (nccl().comm_get_async_error(comm->comm, &async) != ncclSuccess ||
+        (async != ncclSuccess && async != ncclInProgress)) {
+      comm->aborted = true;
+      return SPMV_ERR_NCCL;
+    }
+    const cudaError_t query = cudaStreamQuery(s);
+    if (query == cudaSuccess) return SPMV_OK;
+    if (query != cudaErrorNotReady) return SPMV_ERR_CUDA;
+    if (std::chrono::steady_clock::now() - start > std::chrono::milliseconds(timeout_ms)) {
+      comm->aborted = true;
+      return SPMV_ERR_TIMEOUT;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+}
+// How long a call that drains its own streams waits for collectives before it gives up.
+constexpr int kDrainTimeoutMs = 120000;
+}  // namespace
+
+extern "C" {
+
+// End-to-end products of a row shard from host memory, x split over the ranks: every rank copies its
+// 1/nranks slice of each x in from host memory and the slices are all-gathered in place (one
+// ncclAllGather), then the shard's product runs and its rows of y are copied out. Vectors pipeline over two
+// device buffers and three streams (copies in and the all-gathers on the caller's stream, products on a
+// second, copies out on a third), as spmv_operator_run_host_batch does on one GPU.
+int spmv_shard_run_host_batch(const spmv_operator* shard_op, spmv_comm* comm, const void* x_host, int64_t x_stride,
+                              void* y_host, int64_t y_stride, int count, void* x_device, void* y_device, void* stream) {
+  return guarded([&] {
+    require(shard_op && comm && comm->comm && x_host && y_host && x_device && y_device && count >= 0, "bad arguments");
+    require(!comm->aborted, "the communicator was aborted");
+    spmv_operator_info info;
+    if (spmv_operator_get_info(shard_op, &info) != SPMV_OK) fail(SPMV_ERR_INVALID_ARGUMENT, "bad operator");
+    const int nranks = comm->nranks, rank = comm->rank;
+    const size_t value_bytes = (size_t)value_bytes_of(info.dtype);
+    const int64_t slice = ((int64_t)info.cols + nranks - 1) / nranks;   // x entries a rank copies in
+    const int64_t mine_first = std::min<int64_t>((int64_t)rank * slice, info.cols);
+    const int64_t mine_count = std::min<int64_t>(info.cols, mine_first + slice) - mine_first;
+    const size_t x_pitch = (value_bytes * (size_t)(slice * nranks) + 15) / 16 * 16;
+    const size_t y_bytes = value_bytes * (size_t)info.rows, y_pitch = (y_bytes + 15) / 16 * 16;
+    char* xd = static_cast<char*>(x_device);
+    char* yd = static_cast<char*>(y_device);
+    NcclApi& api = nccl();
+    DeviceScope scope(comm->device);
+    const cudaStream_t copy_in = static_cast<cudaStream_t>(stream);
+    cudaStream_t compute = nullptr, copy_out = nullptr;
+    cudaEvent_t gathered[2] = {}, computed[2] = {}, copied_out[2] = {};
+    cudaError_t status = cudaStreamCreateWithFlags(&compute, cudaStreamNonBlocking);
+    if (status == cudaSuccess) status = cudaStreamCreateWithFlags(&copy_out, cudaStreamNonBlocking);
+    for (int b = 0; b < 2 && status == cudaSuccess; ++b) {
+      status = cudaEventCreateWithFlags(&gathered[b], cudaEventDisableTiming);
+      if (status == cudaSuccess) status = cudaEventCreateWithFlags(&computed[b], cudaEventDisableTiming);
+      if (status == cudaSuccess) status = cudaEventCreateWithFlags(&copied_out[b], cudaEventDisableTiming);
+    }
+    ncclResult_t collective = ncclSuccess;
+    // vector i uses buffers i mod 2: its copy in waits until the product of vector i - 2 has read x, its
+    // product until the copy out of vector i - 2 has read y
+    for (int i = 0; i < count && status == cudaSuccess && collective == ncclSuccess; ++i) {
+      const int b = i & 1;
+      char* x_b = xd + b * x_pitch;
+      const char* xh = static_cast<const char*>(x_host) + (int64_t)i * x_stride;
+      char* yh = static_cast<char*>(y_host) + (int64_t)i * y_stride;
+      if (i >= 2) status = cudaStreamWaitEvent(copy_in, computed[b], 0);
+      if (status == cudaSuccess && mine_count > 0)
+        status = cudaMemcpyAsync(x_b + value_bytes * mine_first, xh + value_bytes * mine_first,
+                                 value_bytes * (size_t)mine_count, cudaMemcpyHostToDevice, copy_in);
+      if (status != cudaSuccess) break;
+      collective = api.all_gather(x_b + value_bytes * (size_t)(rank * slice), x_b, (size_t)slice, nccl_type(info.dtype),
+                                  comm->comm, copy_in);
+      if (collective != ncclSuccess) break;
+      status = cudaEventRecord(gathered[b], copy_in);
+      if (status == cudaSuccess) status = cudaStreamWaitEvent(compute, gathered[b], 0);
+      if (status == cudaSuccess && i >= 2) status = cudaStreamWaitEvent(compute, copied_out[b], 0);
+      if (status == cudaSuccess) status = run_operator_leaving_sms(shard_op, x_b, yd + b * y_pitch, compute, 0);
+      if (status == cudaSuccess) status = cudaEventRecord(computed[b], compute);
+      if (status == cudaSuccess) status = cudaStreamWaitEvent(copy_out, computed[b], 0);
+      if (status == cudaSuccess) status = cudaMemcpyAsync(yh, yd + b * y_pitch, y_bytes, cudaMemcpyDeviceToHost, copy_out);
+      if (status == cudaSuccess) status = cudaEventRecord(copied_out[b], copy_out);
+    }
+    if (status == cudaSuccess && collective == ncclSuccess && count > 0)
+      status = cudaStreamWaitEvent(copy_in, copied_out[(count - 1) & 1], 0);
+    // every stream drains before the call returns, after an error too; a collective that another rank
+    // never joins ends in a timeout (the communicator is then aborted) instead of blocking forever
+    for (cudaStream_t drained : {copy_in, compute, copy_out}) {
+      if (!drained) continue;
+      const int waited = wait_for_stream(comm, drained, kDrainTimeoutMs);
+      if (waited != SPMV_OK && status == cudaSuccess && collective == ncclSuccess) status = cudaErrorLaunchTimeout;
+    }
+    for (int b = 0; b < 2; ++b)
+      for (cudaEvent_t event : {gathered[b], computed[b], copied_out[b]})
+        if (event) cudaEventDestroy(event);
+    if (compute) cudaStreamDestroy(compute);
+    if (copy_out) cudaStreamDestroy(copy_out);
+    nccl_check(collective, "ncclAllGather");
+    if (status != cudaSuccess) fail(SPMV_ERR_CUDA, std::string("sharded products through host buffers: ") + cudaGetErrorString(status));
   });
 }
 

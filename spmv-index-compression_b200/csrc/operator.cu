@@ -178,15 +178,14 @@ int window_capacity(const std::vector<int2>& windows) {
 }
 
 // Physical threads per row P: the fewest that leave a thread at most 28 entries of an average row (one
-// batch of gathers), and at least T/16 (at most 16 lane sums per thread; T/8 for CSR-lp, whose 16-lane
-// variants gather half as deep). A tile then holds 256/P rows (at least 128), so that one pass of the
-// CTA's 256/P row groups covers it. Measured on B200 (CSR-i32): 27-point stencil (27 entries a row)
-// P = 1 at T = 8; random band (33) P = 2; block FEM (64) P = 4.
+// batch of gathers), and at least T/16 (at most 16 lane sums per thread). A tile then holds 256/P rows (at
+// least 128), so that one pass of the CTA's 256/P row groups covers it. Measured on B200 (CSR-i32):
+// 27-point stencil (27 entries a row) P = 1 at T = 8; random band (33) P = 2; block FEM (64) P = 4.
 int choose_physical_tpr(int tpr, int layout, double mean_length) {
+  (void)layout;
   int physical = 1;
   while (physical < tpr && mean_length / physical > 28.0) physical *= 2;
-  const int max_slots = layout == SPMV_LAYOUT_LP ? 8 : 16;
-  while (tpr / physical > max_slots) physical *= 2;
+  while (tpr / physical > 16) physical *= 2;
   return physical;
 }
 
@@ -358,6 +357,14 @@ cudaError_t run_operator_leaving_sms(const spmv_operator* op, const void* x, voi
   KernelArgs a = kernel_args(op, x, y);
   if (op->schedule == SPMV_SCHEDULE_TILES && free_sms > 0 && a.tile_ctas > 0)
     a.tile_ctas = std::max<int64_t>(1, std::min<int64_t>(a.tile_ctas, a.tile_ctas - (int64_t)free_sms * op->resident));
+  return launch_product(op, a, stream);
+}
+cudaError_t run_operator_with_peers(const spmv_operator* op, const void* x, void* y, void* const* peers, int peer_count,
+                                    cudaStream_t stream) {
+  if (peer_count < 0 || peer_count > kMaxPeers) return cudaErrorInvalidValue;
+  KernelArgs a = kernel_args(op, x, y);
+  for (int d = 0; d < peer_count; ++d) a.peers[d] = peers[d];
+  a.peer_count = peer_count;
   return launch_product(op, a, stream);
 }
 }  // namespace spmvb200
@@ -578,8 +585,9 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
       }
     // windows of x: when the gathers are scattered (under 1.5 nonzeros per x sector a row reads) and most
     // tiles read x within at most 24 KB of columns (a random band), every tile stages that window with its
-    // streams and gathers from shared memory; the tiles then shrink to leave room for it. Not for CSR-lp,
-    // whose decode leaves no room (measured slower), nor where gathers come in runs (stencils: slower).
+    // streams and gathers from shared memory; the tiles then shrink to leave room for it. Not for CSR-lp
+    // (measured slower: the decode's gathers then choose their source at run time), nor where gathers come
+    // in runs (stencils: slower).
     const int window_limit = 24 * 1024 / value_bytes;
     std::vector<int2> windows;
     if (!packed && run_length < 1.5) {

@@ -189,6 +189,16 @@ _sig("spmv_comm_destroy", None, _v)
 _sig("spmv_comm_check", _i, _v, _v, _i)
 _sig("spmv_chain_run", _i, _v, _v, _v, _v, _v, _i, _v)
 _sig("spmv_chain_run_blocks", _i, _v, _i, _i, _v, _v, _v, _i, _v)
+_sig("spmv_shard_run_host_batch", _i, _v, _v, _v, _i64, _v, _i64, _i, _v, _v, _v)
+_sig("spmv_peer_group_create", _i, _i, _i, _i64, _i, _c_void_pp)
+_sig("spmv_peer_group_handle", _i, _v, _v)
+_sig("spmv_peer_group_open", _i, _v, _v)
+_sig("spmv_peer_group_x", _i, _v, _i, _c_void_pp)
+_sig("spmv_peer_group_barrier", _i, _v, _i, _v)
+_sig("spmv_peer_group_copy_x", _i, _v, _i, _v, _i64, _v)
+_sig("spmv_peer_group_check", _i, _v)
+_sig("spmv_chain_run_peer", _i, _v, _v, _v, _i, _i, _v)
+_sig("spmv_peer_group_destroy", None, _v)
 
 
 def _check(status: int):
@@ -230,7 +240,7 @@ class CsrMatrix:
 
     def __del__(self):
         handle = getattr(self, "_handle", None)
-        if handle is not None and handle.value:
+        if _lib is not None and handle is not None and handle.value:   # _lib may be gone at interpreter exit
             _lib.spmv_csr_destroy(handle)
             self._handle = None
 
@@ -553,7 +563,8 @@ class Operator:
             self._handle = None
 
     def __del__(self):
-        self.close()
+        if _lib is not None:   # at interpreter exit the module's globals may already be gone
+            self.close()
 
     def __enter__(self):
         return self
@@ -653,7 +664,8 @@ class Comm:
             self._handle = None
 
     def __del__(self):
-        self.close()
+        if _lib is not None:   # at interpreter exit the module's globals may already be gone
+            self.close()
 
 
 def chain_run(shard_op: "Operator", comm: Comm, shard_row_begin, x_current: int, x_next: int, products: int,
@@ -665,6 +677,16 @@ def chain_run(shard_op: "Operator", comm: Comm, shard_row_begin, x_current: int,
                                stream or None))
 
 
+def shard_run_host_batch(shard_op: "Operator", comm: Comm, x_host: int, x_stride: int, y_host: int, y_stride: int,
+                         count: int, x_device: int, y_device: int, stream: int = 0):
+    """count products of this rank's shard from host memory: each rank copies its 1/nranks slice of every
+    x in, the slices are all-gathered over NCCL, the product runs and the shard's rows of y go out.
+    x_device holds two buffers of nranks * ceil(cols / nranks) entries (each rounded up to 16 bytes),
+    y_device two of the shard's rows."""
+    _check(_lib.spmv_shard_run_host_batch(shard_op.handle, comm.handle, x_host, x_stride, y_host, y_stride, count,
+                                          x_device, y_device, stream or None))
+
+
 def chain_run_blocks(block_ops: Sequence["Operator"], block_rows: int, comm: Comm, x_current: int, x_next: int,
                      products: int, stream: int = 0):
     """products chained y -> x over interleaved row blocks: block_ops[c] holds rows of block
@@ -673,6 +695,73 @@ def chain_run_blocks(block_ops: Sequence["Operator"], block_rows: int, comm: Com
     handles = (ctypes.c_void_p * len(block_ops))(*[op.handle.value for op in block_ops])
     _check(_lib.spmv_chain_run_blocks(handles, len(block_ops), block_rows, comm.handle, x_current, x_next, products,
                                       stream or None))
+
+
+class PeerGroup:
+    """One rank's share of chained products over peer memory: two x buffers and barrier flags, mapped by
+    every other rank (CUDA IPC), so that each product stores its rows straight into every rank's next x."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, nranks: int, rank: int, x_bytes: int, device: int = -1):
+        handle = ctypes.c_void_p()
+        _check(_lib.spmv_peer_group_create(nranks, rank, x_bytes, device, ctypes.byref(handle)))
+        self._handle = handle
+        self.nranks, self.rank = nranks, rank
+
+    @property
+    def handle(self):
+        return self._handle
+
+    def export(self) -> bytes:
+        """This rank's allocation handle, to be gathered by every rank in rank order."""
+        out = ctypes.create_string_buffer(self.HANDLE_BYTES)
+        _check(_lib.spmv_peer_group_handle(self._handle, out))
+        return out.raw
+
+    def open(self, handles: Sequence[bytes]):
+        blob = b"".join(handles)
+        if len(blob) != self.HANDLE_BYTES * self.nranks:
+            raise ValueError("one handle per rank is required")
+        _check(_lib.spmv_peer_group_open(self._handle, ctypes.create_string_buffer(blob, len(blob))))
+
+    def x(self, which: int = 0) -> int:
+        """Device pointer of the current x (which=0) or of the other buffer (which=1)."""
+        pointer = ctypes.c_void_p()
+        _check(_lib.spmv_peer_group_x(self._handle, which, ctypes.byref(pointer)))
+        return pointer.value
+
+    def write_x(self, pointer: int, nbytes: int, stream: int = 0):
+        """Copies nbytes from pointer (host or device memory) into this rank's current x."""
+        _check(_lib.spmv_peer_group_copy_x(self._handle, 0, pointer, nbytes, stream or None))
+
+    def read_x(self, pointer: int, nbytes: int, stream: int = 0):
+        """Copies nbytes of this rank's current x to pointer (host or device memory)."""
+        _check(_lib.spmv_peer_group_copy_x(self._handle, 1, pointer, nbytes, stream or None))
+
+    def barrier(self, timeout_ms: int = 5000, stream: int = 0):
+        _check(_lib.spmv_peer_group_barrier(self._handle, timeout_ms, stream or None))
+
+    def check(self):
+        _check(_lib.spmv_peer_group_check(self._handle))
+
+    def close(self):
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            _lib.spmv_peer_group_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        if _lib is not None:   # at interpreter exit the module's globals may already be gone
+            self.close()
+
+
+def chain_run_peer(shard_op: "Operator", group: PeerGroup, shard_row_begin, products: int, stream: int = 0,
+                   timeout_ms: int = 5000):
+    """products chained y -> x over the row shards, each product storing its rows into every rank's next x
+    over peer memory, then a barrier of the ranks' GPUs. The result is the group's current x."""
+    bounds = np.ascontiguousarray(shard_row_begin, dtype=np.int32)
+    _check(_lib.spmv_chain_run_peer(shard_op.handle, group.handle, _pointer(bounds), products, timeout_ms,
+                                    stream or None))
 
 
 def interleaved_block_rows(row_ptr, col_ind, values, nranks: int, blocks_per_rank: int, rank: int):

@@ -1,8 +1,9 @@
 """Chained products over NCCL on two GPUs (spmv_chain_run): each rank's CSR-lp shard product into its
 slice of the next x, the slices all-gathered (grouped broadcasts for nnz-balanced shards of unequal rows,
 one all-gather for equal ones), three times; and over interleaved row blocks whose all-gathers run beside
-the next block's product (spmv_chain_run_blocks); the results bit-identical to the oracle's chain on the
-whole matrix."""
+the next block's product (spmv_chain_run_blocks); and over peer memory, each product storing its rows into
+both GPUs' next x (spmv_chain_run_peer); the results bit-identical to the oracle's chain on the whole
+matrix."""
 import datetime
 import os
 import socket
@@ -70,6 +71,26 @@ def worker(rank, world, port):
         assert np.array_equal(result.view(np.uint64), want.view(np.uint64)), products
     for op in ops:
         op.close()
+    # chained products over peer memory (spmv_chain_run_peer): each product stores its rows into both
+    # ranks' next x, then a barrier of the two GPUs; nnz-balanced and equal shards, 3 products then 1 more
+    group = spmv.PeerGroup(world, rank, x0.nbytes, device=rank)
+    handles = [None] * world
+    dist.all_gather_object(handles, group.export())
+    group.open(handles)
+    stream = torch.cuda.current_stream().cuda_stream
+    for bounds in (spmv.shard_rows(matrix, world), np.array([0, 10000, 20000], dtype=np.int32)):
+        shard = matrix.slice_rows(int(bounds[rank]), int(bounds[rank + 1]))
+        with spmv.Operator(shard, spmv.LP, spmv.F64, 8, device=rank) as op:
+            group.write_x(x0.ctypes.data, x0.nbytes)
+            dist.barrier()
+            for products, want in ((3, expected), (1, fourth)):
+                spmv.chain_run_peer(op, group, bounds, products, stream, timeout_ms=20000)
+                group.check()
+                result = np.empty_like(x0)
+                group.read_x(result.ctypes.data, result.nbytes)
+                assert np.array_equal(result.view(np.uint64), want.view(np.uint64)), (bounds.tolist(), products)
+        dist.barrier()
+    group.close()
     comm.close()
     dist.destroy_process_group()
 
