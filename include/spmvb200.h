@@ -131,6 +131,13 @@ int spmv_csr_reorder_rcm(const char* matrix_path, const spmv_csr* matrix, spmv_c
  * SPMV_ERR_TOO_LARGE if cap is smaller. Requires a square matrix with nnz > 0 (characterize main:314). */
 int spmv_characterize(const spmv_csr* matrix, const char* ordering, double ordering_seconds, char* csv,
                       size_t cap, size_t* needed);
+/* The same CSV computed on the GPU (device ordinal, -1 = current): the per-row metrics (spans, bandwidth,
+ * 8/16-bit fits, lane occupancy, windowed segments, uncached gathers) by one thread per row, the span
+ * percentiles by a radix select on the device; the FIFO gather model, sequential by definition, as twelve
+ * host threads beside the GPU. Byte for byte spmv_characterize's output. No counterpart in the reference
+ * (its tool runs on the host, characterize_matrix.cpp:92-251). */
+int spmv_characterize_device(const spmv_csr* matrix, const char* ordering, double ordering_seconds, int device,
+                             char* csv, size_t cap, size_t* needed);
 
 /* ---- layouts, admissibility and byte model: src/bench_csr_width.cu:149-285 ------------------------ */
 /* MatrixFacts (bench_csr_width.cu:160): widest row span and the CSR-lp word counts by log2(T). */
@@ -204,6 +211,9 @@ typedef struct {
   int tile_rows;          /* rows a tile holds at most, a multiple of 16 (0 = chosen by the library)  */
   int schedule;           /* SPMV_SCHEDULE_*: how rows are mapped to the kernel (0 = chosen by the library) */
   int accumulate;         /* SPMV_ACCUMULATE_*: the type FP16 values are summed in (0 = FP32)             */
+  int mirror;             /* 1: tiles keep an image of their rows of y in shared memory, from which the
+                           * products of spmv_chain_run_peer store them into the other GPUs' copies of x
+                           * (without it those rows are read back from y); 0: none                       */
 } spmv_operator_config;
 
 /* The type a product sums in. WIDE: FP64 values in FP64, FP32 and FP16 values in FP32 (AccumulatorOf,

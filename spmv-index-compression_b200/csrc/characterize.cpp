@@ -7,74 +7,59 @@
 // first-in first-out caches of 0, 8, 32, 128 and 131072 sectors. A FIFO cache holds exactly the last C
 // sectors it inserted (a hit inserts nothing), so a sector is resident when its most recent insertion
 // is among the last C; one array of last-insertion stamps per capacity replaces the hash sets.
-#include "internal.hpp"
+#include "characterize.hpp"
 
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <thread>
 
 namespace spmvb200 {
 
+// measure_gather_traffic (characterize_matrix.cpp:92), one capacity level of one value size.
+int64_t fifo_gather_misses(const Csr& matrix, int value_index, int level) {
+  const int value_bytes = kCharacterizeValueBytes[value_index];
+  const int64_t capacity = kCharacterizeCacheSectors[level];
+  const int64_t sector_count = (int64_t)matrix.cols * value_bytes / kCharacterizeSectorBytes + 1;
+  std::vector<int64_t> stamp((size_t)sector_count, -1);
+  int64_t misses = 0, insertions = 0;
+  for (int row = 0; row < matrix.rows; ++row) {
+    int64_t previous = -1;
+    for (int entry = matrix.row_ptr[row]; entry < matrix.row_ptr[row + 1]; ++entry) {
+      const int64_t sector = (int64_t)matrix.col_ind[entry] * value_bytes / kCharacterizeSectorBytes;
+      if (sector == previous) continue;
+      previous = sector;
+      int64_t& last = stamp[sector];
+      if (last >= 0 && last >= insertions - capacity) continue;
+      ++misses;
+      last = insertions++;
+    }
+  }
+  return misses;
+}
+
 namespace {
 
-constexpr int kValueBytes[3] = {8, 4, 2};
-constexpr int kSectorBytes = 32;
-constexpr int64_t kCacheSectors[5] = {0, 8, 32, 128, 131072};
-constexpr int kThreadsPerRow[5] = {2, 4, 8, 16, 32};
-
-struct Characterization {
-  int64_t empty_rows = 0;
-  int64_t bandwidth = 0;
-  int row_span_max = 0;
-  double row_span_mean = 0.0;
-  int row_span_p50 = 0;
-  int row_span_p90 = 0;
-  double rows_fitting_8bit = 0.0, rows_fitting_16bit = 0.0;
-  double nnz_in_rows_fitting_8bit = 0.0, nnz_in_rows_fitting_16bit = 0.0;
-  int64_t segments_8bit = 0, segments_16bit = 0;
-  double gamma_csr_i32 = 0.0, bytes_per_nnz_csr_i32 = 0.0, bytes_per_nnz_index_free = 0.0;
-  double bytes_per_nnz_rowbase_16 = NAN, bytes_per_nnz_rowbase_8 = NAN;
-  double bytes_per_nnz_windowed_16 = 0.0, bytes_per_nnz_windowed_8 = 0.0;
-  double speedup_ceiling = 0.0, speedup_rowbase_16 = NAN, speedup_rowbase_8 = NAN;
-  double speedup_windowed_16 = 0.0, speedup_windowed_8 = 0.0, working_set_mib_csr_i32 = 0.0;
-  double lane_occupancy[5] = {0, 0, 0, 0, 0};
-  double tail_ratio[5] = {0, 0, 0, 0, 0};
-  double gather_bytes[3][5] = {{0}};
-};
-
-// measure_gather_traffic (characterize_matrix.cpp:92).
-void gather_traffic(const Csr& matrix, Characterization& result) {
-  for (int value_index = 0; value_index < 3; ++value_index) {
-    const int value_bytes = kValueBytes[value_index];
-    const int64_t sector_count = (int64_t)matrix.cols * value_bytes / kSectorBytes + 1;
-    std::vector<int64_t> stamp[5];
-    int64_t misses[5] = {0, 0, 0, 0, 0};
-    int64_t insertions[5] = {0, 0, 0, 0, 0};
-    for (int level = 1; level < 5; ++level) stamp[level].assign((size_t)sector_count, -1);
-    for (int row = 0; row < matrix.rows; ++row) {
-      int64_t previous = -1;
-      for (int entry = matrix.row_ptr[row]; entry < matrix.row_ptr[row + 1]; ++entry) {
-        const int64_t sector = (int64_t)matrix.col_ind[entry] * value_bytes / kSectorBytes;
-        if (sector == previous) continue;
-        previous = sector;
-        ++misses[0];
-        for (int level = 1; level < 5; ++level) {
-          int64_t& last = stamp[level][sector];
-          if (last >= 0 && last >= insertions[level] - kCacheSectors[level]) continue;
-          ++misses[level];
-          last = insertions[level]++;
-        }
-      }
+// The sectors a row-by-row gather touches without a cache (gather level 0): distinct sectors in a row's
+// run of equal sectors count once.
+int64_t uncached_gathers(const Csr& matrix, int value_index) {
+  const int value_bytes = kCharacterizeValueBytes[value_index];
+  int64_t misses = 0;
+  for (int row = 0; row < matrix.rows; ++row) {
+    int64_t previous = -1;
+    for (int entry = matrix.row_ptr[row]; entry < matrix.row_ptr[row + 1]; ++entry) {
+      const int64_t sector = (int64_t)matrix.col_ind[entry] * value_bytes / kCharacterizeSectorBytes;
+      if (sector != previous) ++misses;
+      previous = sector;
     }
-    for (int level = 0; level < 5; ++level)
-      result.gather_bytes[value_index][level] = (double)misses[level] * kSectorBytes / (double)matrix.nnz();
   }
+  return misses;
 }
 
 // measure_lane_occupancy (characterize_matrix.cpp:139).
 void lane_occupancy(const Csr& matrix, Characterization& result) {
   for (int index = 0; index < 5; ++index) {
-    const int threads = kThreadsPerRow[index];
+    const int threads = kCharacterizeThreadsPerRow[index];
     int64_t occupied = 0, iterations = 0, longest = 0;
     for (int row = 0; row < matrix.rows; ++row) {
       const int length = matrix.row_ptr[row + 1] - matrix.row_ptr[row];
@@ -133,6 +118,18 @@ void row_spans(const Csr& matrix, Characterization& result) {
   result.row_span_p90 = spans[(size_t)(0.90 * (spans.size() - 1))];
 }
 
+}  // namespace
+
+void characterize_rows(const Csr& matrix, Characterization& result) {
+  row_spans(matrix, result);
+  lane_occupancy(matrix, result);
+  for (int value_index = 0; value_index < 3; ++value_index)
+    result.gather_bytes[value_index][0] =
+        (double)uncached_gathers(matrix, value_index) * kCharacterizeSectorBytes / (double)matrix.nnz();
+  result.segments_8bit = windowed_segments(matrix, 256);
+  result.segments_16bit = windowed_segments(matrix, 65536);
+}
+
 // apply_byte_model (characterize_matrix.cpp:225): FP64 values, int32 row pointer.
 void byte_model(const Csr& matrix, Characterization& result) {
   const double value_bytes = 8.0, pointer_bytes = 4.0, nnz = (double)matrix.nnz();
@@ -155,19 +152,8 @@ void byte_model(const Csr& matrix, Characterization& result) {
   result.working_set_mib_csr_i32 = result.bytes_per_nnz_csr_i32 * nnz / 1048576.0;
 }
 
-}  // namespace
-
-std::string characterize(const Csr& matrix, const std::string& ordering, double ordering_seconds) {
-  if (matrix.rows != matrix.cols || matrix.nnz() == 0) fail(SPMV_ERR_INVALID_ARGUMENT, "not square or empty");
-  if (ordering != "original" && ordering != "rcm") fail(SPMV_ERR_INVALID_ARGUMENT, "ordering must be original or rcm");
-  Characterization result;
-  row_spans(matrix, result);
-  lane_occupancy(matrix, result);
-  gather_traffic(matrix, result);
-  result.segments_8bit = windowed_segments(matrix, 256);
-  result.segments_16bit = windowed_segments(matrix, 65536);
-  byte_model(matrix, result);
-
+std::string characterization_csv(const Csr& matrix, const Characterization& r, const std::string& ordering,
+                                 double ordering_seconds) {
   const char* header =
       "name,rows,cols,nnz,row_length_mean,row_length_max,row_length_std,empty_rows,bandwidth,"
       "row_span_max,row_span_mean,row_span_p50,row_span_p90,rows_fitting_8bit,rows_fitting_16bit,"
@@ -181,7 +167,6 @@ std::string characterize(const Csr& matrix, const std::string& ordering, double 
       "gather_v8_c0,gather_v8_c8,gather_v8_c32,gather_v8_c128,gather_v8_cl2,"
       "gather_v4_c0,gather_v4_c8,gather_v4_c32,gather_v4_c128,gather_v4_cl2,"
       "gather_v2_c0,gather_v2_c8,gather_v2_c32,gather_v2_c128,gather_v2_cl2\n";
-  const Characterization& r = result;
   std::vector<char> line(4096 + matrix.name.size() * 2);
   std::snprintf(line.data(), line.size(),
       "%s,%d,%d,%lld,%.4f,%d,%.4f,%lld,%lld,%d,%.2f,%d,%d,%.6f,%.6f,%.6f,%.6f,%lld,%lld,"
@@ -202,6 +187,19 @@ std::string characterize(const Csr& matrix, const std::string& ordering, double 
       r.gather_bytes[1][0], r.gather_bytes[1][1], r.gather_bytes[1][2], r.gather_bytes[1][3], r.gather_bytes[1][4],
       r.gather_bytes[2][0], r.gather_bytes[2][1], r.gather_bytes[2][2], r.gather_bytes[2][3], r.gather_bytes[2][4]);
   return std::string(header) + line.data();
+}
+
+std::string characterize(const Csr& matrix, const std::string& ordering, double ordering_seconds) {
+  if (matrix.rows != matrix.cols || matrix.nnz() == 0) fail(SPMV_ERR_INVALID_ARGUMENT, "not square or empty");
+  if (ordering != "original" && ordering != "rcm") fail(SPMV_ERR_INVALID_ARGUMENT, "ordering must be original or rcm");
+  Characterization result;
+  characterize_rows(matrix, result);
+  for (int value_index = 0; value_index < 3; ++value_index)
+    for (int level = 1; level < 5; ++level)
+      result.gather_bytes[value_index][level] =
+          (double)fifo_gather_misses(matrix, value_index, level) * kCharacterizeSectorBytes / (double)matrix.nnz();
+  byte_model(matrix, result);
+  return characterization_csv(matrix, result, ordering, ordering_seconds);
 }
 
 }  // namespace spmvb200

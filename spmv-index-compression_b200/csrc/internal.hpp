@@ -70,6 +70,8 @@ Csr reorder_with_rcm(const std::string& matrix_path, const Csr& matrix, double& 
 
 // characterize.cpp
 std::string characterize(const Csr& matrix, const std::string& ordering, double ordering_seconds);
+// characterize_device.cu: the same text with the per-row metrics computed on the current GPU
+std::string characterize_device(const Csr& matrix, const std::string& ordering, double ordering_seconds);
 
 // layouts.cpp
 struct Facts {

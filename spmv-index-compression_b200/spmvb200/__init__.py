@@ -93,7 +93,7 @@ class OperatorConfig(ctypes.Structure):
     _fields_ = [("layout", ctypes.c_int), ("dtype", ctypes.c_int), ("tpr", ctypes.c_int),
                 ("physical_tpr", ctypes.c_int), ("tile_nnz", ctypes.c_int), ("value_rounding", ctypes.c_int),
                 ("device", ctypes.c_int), ("stages", ctypes.c_int), ("tile_rows", ctypes.c_int),
-                ("schedule", ctypes.c_int), ("accumulate", ctypes.c_int)]
+                ("schedule", ctypes.c_int), ("accumulate", ctypes.c_int), ("mirror", ctypes.c_int)]
 
 
 class OperatorInfo(ctypes.Structure):
@@ -153,6 +153,7 @@ _sig("spmv_permutation_write", _i, _s, _v, _i64, _d)
 _sig("spmv_permutation_read", _i, _s, _i, _v, ctypes.POINTER(_d), _c_int_p)
 _sig("spmv_csr_reorder_rcm", _i, _s, _v, _c_void_pp, ctypes.POINTER(_d))
 _sig("spmv_characterize", _i, _v, _s, _d, _v, _sz, ctypes.POINTER(_sz))
+_sig("spmv_characterize_device", _i, _v, _s, _d, _i, _v, _sz, ctypes.POINTER(_sz))
 _sig("spmv_matrix_facts", _i, _v, ctypes.POINTER(Facts))
 _sig("spmv_admissible", _i, _v, ctypes.POINTER(Facts), _i, _i, _c_int_p)
 _sig("spmv_memory_of", _i, _v, ctypes.POINTER(Facts), _i, _i, _i, ctypes.POINTER(MemoryBreakdown))
@@ -351,6 +352,16 @@ def reorder_with_rcm(matrix_path: str, matrix: CsrMatrix):
     return CsrMatrix(handle.value), seconds.value
 
 
+def characterize_device(matrix: CsrMatrix, ordering: str = "original", ordering_seconds: float = 0.0,
+                        device: int = -1) -> str:
+    """characterize() computed on the GPU (the FIFO gather model on host threads beside it); the same text."""
+    capacity = ctypes.c_size_t(8192 + 2 * len(matrix.name.encode()))
+    buffer = ctypes.create_string_buffer(capacity.value)
+    _check(_lib.spmv_characterize_device(matrix.handle, ordering.encode(), ordering_seconds, device, buffer,
+                                         capacity.value, None))
+    return buffer.value.decode()
+
+
 def characterize(matrix: CsrMatrix, ordering: str = "original", ordering_seconds: float = 0.0) -> str:
     """The header and value line of src/characterize_matrix.cpp:253 (write_csv)."""
     needed = ctypes.c_size_t()
@@ -539,7 +550,7 @@ class Operator:
 
     def __init__(self, matrix: CsrMatrix, layout: int, dtype: int, tpr: int, physical_tpr: int = 0,
                  tile_nnz: int = 0, value_rounding: int = 0, device: int = -1, stages: int = 0, tile_rows: int = 0,
-                 schedule: int = 0, accumulate: int = 0):
+                 schedule: int = 0, accumulate: int = 0, mirror: int = 0):
         config = OperatorConfig()
         _lib.spmv_operator_config_init(ctypes.byref(config), layout, dtype, tpr)
         config.physical_tpr = physical_tpr
@@ -550,6 +561,7 @@ class Operator:
         config.tile_rows = tile_rows
         config.schedule = schedule
         config.accumulate = accumulate
+        config.mirror = mirror
         handle = ctypes.c_void_p()
         _check(_lib.spmv_operator_create(matrix.handle, ctypes.byref(config), ctypes.byref(handle)))
         self._handle = handle
