@@ -539,7 +539,7 @@ def chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threa
         if not spmv.configuration_admissible(shard, facts, spmv.Configuration.of(layout, dtype, tpr)):
             out["layouts"][name] = {"status": "not admissible"}
             continue
-        op = spmv.Operator(shard, layout, dtype, tpr, device=local_rank, mirror=1)
+        op = spmv.Operator(shard, layout, dtype, tpr, device=local_rank)
         info = op.info()
         # one chained product from x0, its rows checked against the oracle on a block of this rank's rows and
         # on the first rows of the next rank's shard (rows that reached this rank through its peers' stores);

@@ -211,9 +211,6 @@ typedef struct {
   int tile_rows;          /* rows a tile holds at most, a multiple of 16 (0 = chosen by the library)  */
   int schedule;           /* SPMV_SCHEDULE_*: how rows are mapped to the kernel (0 = chosen by the library) */
   int accumulate;         /* SPMV_ACCUMULATE_*: the type FP16 values are summed in (0 = FP32)             */
-  int mirror;             /* 1: tiles keep an image of their rows of y in shared memory, from which the
-                           * products of spmv_chain_run_peer store them into the other GPUs' copies of x
-                           * (without it those rows are read back from y); 0: none                       */
 } spmv_operator_config;
 
 /* The type a product sums in. WIDE: FP64 values in FP64, FP32 and FP16 values in FP32 (AccumulatorOf,

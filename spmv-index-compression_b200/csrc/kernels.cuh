@@ -126,12 +126,10 @@ struct KernelArgs {
                              // CTAs per multiprocessor (kDenseResidency)
   unsigned* status;          // device status word (may be null)
   // copies of y in other GPUs' memory (peer pointers, indexed by the same rows as y): every row's result is
-  // stored there too, so that a chained product's all-gather happens inside the product. The tile kernel
-  // stores a tile's rows into them once the tile is done, in runs of consecutive rows.
+  // stored there too, by the thread that stores it into y, so that a chained product's all-gather happens
+  // inside the product
   void* peers[kMaxPeers];
   int peer_count;
-  int mirror_rows;           // k_spmv_tiles: rows of each stage's image of y (0: none; the rows are then read back
-                             // from y for the stores into the peers)
   // k_spmv_classes (rows by length): long-row blocks, then the blocks of each segment of listed rows
   // (P = 32, 16, ..., 1 threads per row), then the short-row blocks
   const int4* row_items;     // {row, first entry, end entry, row base} of the listed rows, by segment
@@ -147,7 +145,7 @@ struct KernelArgs {
 // row_width slices and of its value and index (or CSR-lp word) ranges. An image starts at the 16-byte
 // boundary at or below its first element, so it holds up to 16 bytes before and after the range.
 struct StagePlan {
-  int header, row_ptr, row_base, row_word, row_width, values, index, window, mirror, bytes;
+  int header, row_ptr, row_base, row_word, row_width, values, index, window, bytes;
 };
 
 __host__ __device__ inline int round16(int bytes) { return (bytes + 15) & ~15; }
@@ -155,10 +153,8 @@ __host__ __device__ inline int round16(int bytes) { return (bytes + 15) & ~15; }
 // index_words: CSR-lp, the words a tile's stream image holds at most (the longest tile's word range plus
 // the word a delta may read past it); ignored by the other layouts, whose index image holds tile_nnz.
 // window_elements: the x elements a tile's window of x holds at most (0: no window).
-// mirror_rows: the results a tile's image of y holds (its rows, for the stores into other GPUs' copies of y;
-// 0: no image).
 __host__ __device__ inline StagePlan stage_plan(int tile_nnz, int tile_rows, int value_bytes, int layout, int index_words,
-                                                int window_elements, int mirror_rows) {
+                                                int window_elements) {
   const bool base = layout == SPMV_LAYOUT_R16 || layout == SPMV_LAYOUT_R8 || layout == SPMV_LAYOUT_LP;
   const bool packed = layout == SPMV_LAYOUT_LP;
   const int index_bytes = packed ? 4 : (layout == SPMV_LAYOUT_I32 ? 4 : ((layout == SPMV_LAYOUT_I16 || layout == SPMV_LAYOUT_R16) ? 2 : 1));
@@ -172,14 +168,13 @@ __host__ __device__ inline StagePlan stage_plan(int tile_nnz, int tile_rows, int
   plan.values = offset;    offset += round16(value_bytes * tile_nnz) + 16;
   plan.index = offset;     offset += packed ? round16(4 * index_words) + 16 : round16(index_bytes * tile_nnz) + 16;
   plan.window = offset;    if (window_elements > 0) offset += round16(value_bytes * window_elements) + 32;
-  plan.mirror = offset;    if (mirror_rows > 0) offset += round16(value_bytes * mirror_rows);
   plan.bytes = offset;
   return plan;
 }
 
 __host__ __device__ inline int tile_smem_bytes(int tile_nnz, int tile_rows, int value_bytes, int layout, int stages,
-                                               int index_words, int window_elements, int mirror_rows) {
-  return 64 + stages * stage_plan(tile_nnz, tile_rows, value_bytes, layout, index_words, window_elements, mirror_rows).bytes;
+                                               int index_words, int window_elements) {
+  return 64 + stages * stage_plan(tile_nnz, tile_rows, value_bytes, layout, index_words, window_elements).bytes;
 }
 
 // ---- small device helpers -----------------------------------------------------------------------
@@ -338,29 +333,12 @@ __device__ __forceinline__ void mirror_row(const KernelArgs& a, int row, V value
   for (int d = 0; d < a.peer_count; ++d) reinterpret_cast<B*>(a.peers[d])[row] = bits;
 }
 
-// Rows [row_begin, row_end) of y, stored by the warps of this CTA, into every peer's copy: one warp, 32
-// consecutive rows per store (a 128-byte write for 4-byte values). The loads read what the other warps
-// stored (they released the tile after a block-scope fence), so they go past the read-only path.
-template <class V>
-__device__ __forceinline__ void mirror_rows(const KernelArgs& a, int row_begin, int row_end) {
-  using B = typename BitsOf<sizeof(V)>::type;
-  const volatile B* y = reinterpret_cast<const volatile B*>(a.y);
-  for (int row = row_begin + (int)(threadIdx.x & 31); row < row_end; row += 32) {
-    const B bits = y[row];
-    for (int d = 0; d < a.peer_count; ++d) reinterpret_cast<B*>(a.peers[d])[row] = bits;
-  }
-}
-
-// Rows [row_begin, row_end) from a tile's image of y in shared memory (element i: row row_begin + i) into
-// every peer's copy: one warp, 32 consecutive rows per store.
-template <class V>
-__device__ __forceinline__ void mirror_rows_from_image(const KernelArgs& a, const unsigned char* image, int row_begin,
-                                                       int row_end) {
-  using B = typename BitsOf<sizeof(V)>::type;
-  const B* rows = reinterpret_cast<const B*>(image);
-  for (int row = row_begin + (int)(threadIdx.x & 31); row < row_end; row += 32) {
-    const B bits = rows[row - row_begin];
-    for (int d = 0; d < a.peer_count; ++d) reinterpret_cast<B*>(a.peers[d])[row] = bits;
+// Every peer copy of y is visible to the other GPUs before the kernel counts as done: after the CTA's
+// barrier one thread fences at system scope (cumulative over the CTA's stores it synchronised with).
+__device__ __forceinline__ void publish_peer_rows(const KernelArgs& a) {
+  if (a.peer_count > 0) {
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
   }
 }
 
@@ -722,16 +700,6 @@ constexpr int kGathers = SPMV_TILE_GATHERS;
 template <class V>
 struct DenseResidency { static constexpr int value = sizeof(V) == 8 ? 3 : 4; };
 
-// A tile row's result into y and, when this launch stores into other GPUs' copies of y through the stage's
-// image of y, into the image as well (element `local`: the row's place in the tile).
-template <class V>
-__device__ __forceinline__ void store_result(const KernelArgs& a, const unsigned char* stage, const StagePlan& plan, V* y,
-                                             int row, int local, V value) {
-  y[row] = value;
-  if (a.peer_count > 0 && a.mirror_rows > 0)
-    reinterpret_cast<V*>(const_cast<unsigned char*>(stage) + plan.mirror)[local] = value;
-}
-
 template <class V, int LAYOUT, int T, int P, int W>
 __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned char* stage, const StagePlan& plan) {
   using VT = ValueTraits<V>;
@@ -784,7 +752,11 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
         }
       }
       const Acc sum = reduce_lanes<VT, Acc, T, P>(acc);
-      if (p == 0 && active) store_result(a, stage, plan, y, row, local, VT::narrow(sum));
+      if (p == 0 && active) {
+        const V result = VT::narrow(sum);
+        y[row] = result;
+        mirror_row(a, row, result);
+      }
     } else {
       // CSR-lp: a row of at most R rounds decoded lane by lane with all its gathers at once, a longer row
       // round by round
@@ -807,7 +779,11 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
           packed_lanes_in_turn<V, T, P>(tile, x, row, begin, end - begin, base, p, acc);
       }
       const Acc sum = reduce_lanes<VT, Acc, T, P>(acc);
-      if (p == 0 && active) store_result(a, stage, plan, y, row, local, VT::narrow(sum));
+      if (p == 0 && active) {
+        const V result = VT::narrow(sum);
+        y[row] = result;
+        mirror_row(a, row, result);
+      }
     }
   }
 }
@@ -1194,8 +1170,7 @@ __global__ void __launch_bounds__(kTileBlock, 4) k_spmv_classes(const KernelArgs
           run_segment<V, LAYOUT, T, 1>(a, block) || run_segment<V, LAYOUT, T, 0>(a, block)))
       short_rows<V, LAYOUT, T>(a, block);
   }
-  // rows stored into other GPUs' memory are visible there before the kernel counts as done
-  if (a.peer_count > 0) __threadfence_system();
+  publish_peer_rows(a);
 }
 
 // ---- k_spmv_tiles --------------------------------------------------------------------------------------
@@ -1210,14 +1185,13 @@ __global__ void __launch_bounds__(kTileBlock, W) k_spmv_tiles(const KernelArgs a
   extern __shared__ __align__(128) unsigned char smem[];
   if ((int64_t)blockIdx.x < a.vector_blocks) {   // rows longer than a tile, scheduled first
     long_rows<V, LAYOUT, T>(a, smem, blockIdx.x, a.vector_blocks);
-    if (a.peer_count > 0) __threadfence_system();
+    publish_peer_rows(a);
     return;
   }
   __shared__ int s_abort;
   __shared__ int s_released[kMaxStages];   // warps done with the buffer's current tile
   __shared__ int s_fills[kMaxStages];      // bulk fills issued into the buffer so far
-  const StagePlan plan = stage_plan(a.tile_nnz, a.tile_rows, (int)sizeof(V), LAYOUT, a.tile_index_words, a.window_elements,
-                                    a.mirror_rows);
+  const StagePlan plan = stage_plan(a.tile_nnz, a.tile_rows, (int)sizeof(V), LAYOUT, a.tile_index_words, a.window_elements);
   const int stages = a.stages;
   const int64_t cta = (int64_t)blockIdx.x - a.vector_blocks;
   const int64_t ctas = (int64_t)gridDim.x - a.vector_blocks;
@@ -1250,33 +1224,20 @@ __global__ void __launch_bounds__(kTileBlock, W) k_spmv_tiles(const KernelArgs a
     if (__shfl_sync(0xffffffffu, *(volatile int*)&s_abort, 0)) break;
     process_tile<V, LAYOUT, T, P, W>(a, buffers + s * plan.bytes, plan);
     __syncwarp();
-    int last_out = 0;
     if ((threadIdx.x & 31) == 0) {
-      __threadfence_block();   // this warp's reads of the buffer (and its rows of y) happen before its release
+      __threadfence_block();   // this warp's reads of the buffer happen before its release
       if (atomicAdd(&s_released[s], 1) == kWarps - 1) {
-        last_out = 1;
         __threadfence_block();
         s_released[s] = 0;
-      }
-    }
-    if (__shfl_sync(0xffffffffu, last_out, 0)) {
-      if (a.peer_count > 0) {
-        // the last warp out stores the tile's rows of y into the peers' copies, in runs of consecutive rows:
-        // from the stage's image of y, before the buffer is refilled, or read back from y
-        const int4 tile = __ldg(a.tiles + cta + k * ctas);
-        if (a.mirror_rows > 0) mirror_rows_from_image<V>(a, buffers + s * plan.bytes + plan.mirror, tile.x, tile.y);
-        else mirror_rows<V>(a, tile.x, tile.y);
-        __syncwarp();
-      }
-      if ((threadIdx.x & 31) == 0 && k + stages < my_tiles) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        issue_tile<V, LAYOUT>(a, cta + (k + stages) * ctas, buffers + s * plan.bytes, plan, full0 + 8 * s);
-        atomicAdd(&s_fills[s], 1);
+        if (k + stages < my_tiles) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue_tile<V, LAYOUT>(a, cta + (k + stages) * ctas, buffers + s * plan.bytes, plan, full0 + 8 * s);
+          atomicAdd(&s_fills[s], 1);
+        }
       }
     }
   }
-  // rows stored into other GPUs' memory are visible there before the kernel counts as done
-  if (a.peer_count > 0) __threadfence_system();
+  publish_peer_rows(a);
   __syncthreads();
   if (threadIdx.x == 0 && s_abort) {
     // after an abort: wait, bounded, for each buffer's last fill before the CTA's shared memory is released

@@ -272,7 +272,6 @@ struct spmv_operator {
   int2* tile_windows = nullptr;   // tiles: the x window each tile stages, {first, end} column (first == end: none)
   int window_elements = 0;
   int resident = 1;   // tiles: persistent CTAs per multiprocessor
-  int mirror_rows = 0; // tiles: rows of each stage's image of y (peer stores of chained products), 0: none
   bool dense = false; // tiles: the dense variant (one thread per lane, more CTAs per multiprocessor)
   int64_t segment_first[6] = {0, 0, 0, 0, 0, 0};
   int64_t segment_items[6] = {0, 0, 0, 0, 0, 0};
@@ -320,7 +319,6 @@ KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   a.stages = op->stages;
   a.tile_ctas = op->tile_ctas;
   a.dense = op->dense ? 1 : 0;
-  a.mirror_rows = op->mirror_rows;
   a.row_list = op->long_rows;
   a.row_count = op->long_count;
   a.vector_blocks = op->long_ctas;
@@ -399,7 +397,6 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
             "accumulate must be SPMV_ACCUMULATE_WIDE or SPMV_ACCUMULATE_HALF");
     require(config->accumulate == SPMV_ACCUMULATE_WIDE || dtype == SPMV_F16,
             "SPMV_ACCUMULATE_HALF applies to FP16 values only");
-    require(config->mirror == 0 || config->mirror == 1, "mirror must be 0 or 1");
     // the kernel family: FP16 sums in FP16 have their own instantiation
     const int kernel = config->accumulate == SPMV_ACCUMULATE_HALF ? kKernelHalfSums : dtype;
     int device_count = 0;
@@ -574,11 +571,9 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     auto plan_for = [&](int tile_nnz) {
       return plan_tiles(m, tile_nnz, op->tile_rows, packed ? row_word.data() : nullptr, packed ? row_width.data() : nullptr);
     };
-    // operators made for chained products over peer memory keep an image of each tile's rows of y
-    op->mirror_rows = config->mirror ? op->tile_rows : 0;
     auto smem_for = [&](int tile_nnz, const TilePlan* plan, int window_elements) {
       return tile_smem_bytes(tile_nnz, op->tile_rows, value_bytes, layout, op->stages, plan ? plan->index_words : 0,
-                             window_elements, op->mirror_rows);
+                             window_elements);
     };
     if (config->tile_nnz == 0 && !packed)
       while (op->tile_nnz > 256 && smem_for(op->tile_nnz, nullptr, 0) > budget) op->tile_nnz -= 256;

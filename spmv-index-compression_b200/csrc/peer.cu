@@ -3,10 +3,13 @@
 // Every rank (one process per GPU) holds one allocation of its own: two x buffers (the current x and the
 // next) and a block of barrier flags, exported to the other ranks by CUDA IPC and mapped by each of them.
 // A chained product on rank r runs its row shard with y = its rows of the next x, and the product kernel
-// also stores those rows into every other rank's next x through the mapped peer pointers (the tile kernel
-// stores a finished tile's rows in runs of consecutive rows: 128-byte writes for FP32). So when every
-// rank's product is done, every rank's next x is whole: the all-gather took no collective library, no
-// multiprocessors of its own and no pass over x after the product. A barrier between the ranks' GPUs then
+// also stores those rows into every other rank's next x through the mapped peer pointers: the thread that
+// stores a row's result into y stores it into each peer as well, and each CTA ends with one system-scope
+// fence. So when every rank's product is done, every rank's next x is whole: the all-gather took no
+// collective library, no multiprocessors of its own and no pass over x after the product. (Measured on two
+// B200s, block FEM, 16 M rows a rank: 1.858 ms a step against 1.746 ms for the product alone, and 1.92 ms
+// for the product followed by an NCCL all-gather; a tile's rows stored into the peers by the last warp out
+// of the tile cost 0.2 ms more, the same with the peers' buffers replaced by local ones.) A barrier between the ranks' GPUs then
 // closes the product: each rank stores the barrier's epoch into its slot of every rank's flags (a release
 // store at system scope) and waits until its own flags all hold it (acquire loads), for a bounded time
 // after which it sets the group's status word. The barrier orders both ways: no rank reads the next x

@@ -93,7 +93,7 @@ class OperatorConfig(ctypes.Structure):
     _fields_ = [("layout", ctypes.c_int), ("dtype", ctypes.c_int), ("tpr", ctypes.c_int),
                 ("physical_tpr", ctypes.c_int), ("tile_nnz", ctypes.c_int), ("value_rounding", ctypes.c_int),
                 ("device", ctypes.c_int), ("stages", ctypes.c_int), ("tile_rows", ctypes.c_int),
-                ("schedule", ctypes.c_int), ("accumulate", ctypes.c_int), ("mirror", ctypes.c_int)]
+                ("schedule", ctypes.c_int), ("accumulate", ctypes.c_int)]
 
 
 class OperatorInfo(ctypes.Structure):
@@ -550,7 +550,7 @@ class Operator:
 
     def __init__(self, matrix: CsrMatrix, layout: int, dtype: int, tpr: int, physical_tpr: int = 0,
                  tile_nnz: int = 0, value_rounding: int = 0, device: int = -1, stages: int = 0, tile_rows: int = 0,
-                 schedule: int = 0, accumulate: int = 0, mirror: int = 0):
+                 schedule: int = 0, accumulate: int = 0):
         config = OperatorConfig()
         _lib.spmv_operator_config_init(ctypes.byref(config), layout, dtype, tpr)
         config.physical_tpr = physical_tpr
@@ -561,7 +561,6 @@ class Operator:
         config.tile_rows = tile_rows
         config.schedule = schedule
         config.accumulate = accumulate
-        config.mirror = mirror
         handle = ctypes.c_void_p()
         _check(_lib.spmv_operator_create(matrix.handle, ctypes.byref(config), ctypes.byref(handle)))
         self._handle = handle

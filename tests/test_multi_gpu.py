@@ -80,7 +80,7 @@ def worker(rank, world, port):
     stream = torch.cuda.current_stream().cuda_stream
     for bounds in (spmv.shard_rows(matrix, world), np.array([0, 10000, 20000], dtype=np.int32)):
         shard = matrix.slice_rows(int(bounds[rank]), int(bounds[rank + 1]))
-        with spmv.Operator(shard, spmv.LP, spmv.F64, 8, device=rank, mirror=int(bounds[1] == 10000)) as op:
+        with spmv.Operator(shard, spmv.LP, spmv.F64, 8, device=rank) as op:
             group.write_x(x0.ctypes.data, x0.nbytes)
             dist.barrier()
             for products, want in ((3, expected), (1, fourth)):
