@@ -72,6 +72,9 @@ def parse_args():
                         help="chained: n of the block-FEM matrix (a multiple of 8; smaller n for quick runs)")
     parser.add_argument("--chain-layouts", default="i32,lp", help="chained: layouts, comma-separated")
     parser.add_argument("--chain-tpr", type=int, default=8)
+    parser.add_argument("--chain-exchange", choices=("halo", "push"), default="halo",
+                        help="chained: each product pulls only the entries of x its rows read from the other ranks "
+                             "(halo), or stores its rows into every rank's next x (push)")
     parser.add_argument("--no-sweep", action="store_true", help="skip the per-layout/T table and comparators")
     parser.add_argument("--no-chained", action="store_true", help="skip the chained block-FEM products")
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget")
@@ -504,9 +507,11 @@ def run_ours(args, rank, world, local_rank):
 
 def chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threads):
     """Config 5: the block-FEM matrix row-sharded over the ranks (each rank builds only its rows), K chained
-    products y -> x. Each product stores the rank's rows of y into every rank's next x over NVLink peer
-    memory (spmv_chain_run_peer), then a barrier of the GPUs; the product kernels alone are timed too, and
-    one more product is checked on a block of each rank's rows against the oracle."""
+    products y -> x over NVLink peer memory (spmv_chain_run_peer), each followed by a barrier of the GPUs.
+    The exchange is the halo (each product pulls only the entries of the next x its rows read from the
+    other ranks) or the push (each product stores its rows into every rank's next x). The product kernels
+    alone are timed too, and two chained products are checked against the oracle on a block of each rank's
+    rows whose columns reach into the previous rank's rows."""
     dtype = spmv.F32
     tpr = args.chain_tpr
     bounds = fem_bounds(world)
@@ -518,21 +523,29 @@ def chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threa
     group = spmv.PeerGroup(world, rank, x_host.nbytes, device=local_rank)
     if world > 1:
         group.open(ranks.gather_objects(group.export(), world))
+    halo_entries = group.set_halo(shard, bounds) if args.chain_exchange == "halo" else None
     peak, _ = measured_peak()
     total_nnz = 64 * FEM_ROWS
-    sample_rows = min(65536, last - first)
+    # the parity block: the first rows of this rank's shard; their columns reach into the previous rank's rows,
+    # so their second chained product reads entries of the first that came through the exchange
+    sample_rows = min(4096, last - first)
     sample = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, first, first + sample_rows)
     s_ptr, s_col, s_val = sample.arrays()
-    # the first rows of the next rank's shard, which reach this rank only through the peers' stores
-    peer_first = int(bounds[(rank + 1) % world])
-    peer_rows = min(65536, int(bounds[(rank + 1) % world + 1]) - peer_first)
-    peer_sample = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, peer_first, peer_first + peer_rows)
-    p_ptr, p_col, p_val = peer_sample.arrays()
+    reach = (int(s_col.min()), int(s_col.max()) + 1)   # the entries of the first product the block reads
+    around = spmv.synth_block_fem(FEM_ROWS, 8, 8, 50_000, 4, reach[0], reach[1])
+    a_ptr, a_col, a_val = around.arrays()
+    x_first = x_host.copy()
+    x_first[reach[0]:reach[1]] = oracle_product(a_ptr, a_col, a_val, x_host, dtype, tpr, threads)
+    x_second_block = oracle_product(s_ptr, s_col, s_val, x_first, dtype, tpr, threads)
     out = {"workload": WORKLOADS["fem"].replace("n=32M", f"n={FEM_ROWS}"), "rows": FEM_ROWS, "nnz": total_nnz,
-           "tpr": tpr, "steps": args.steps, "warmup": args.warmup, "n_gpus": world,
-           "parallelism": f"row shards x{world} (block-aligned, equal nonzeros); every product stores its rows into "
-                          "every rank's next x over NVLink peer memory, then a barrier of the GPUs",
+           "tpr": tpr, "steps": args.steps, "warmup": args.warmup, "n_gpus": world, "exchange": args.chain_exchange,
+           "parallelism": f"row shards x{world} (block-aligned, equal nonzeros); " + (
+               f"each product pulls the {halo_entries} entries of the next x its rows read from the other ranks' memory"
+               if args.chain_exchange == "halo" else
+               "each product stores its rows into every rank's next x") + " over NVLink, after a barrier of the GPUs",
            "layouts": {}}
+    if halo_entries is not None:
+        out["halo_entries_per_rank"] = halo_entries
     y_alone = torch.empty(last - first, dtype=torch.float32, device=f"cuda:{local_rank}")
     for name in [item for item in args.chain_layouts.split(",") if item]:
         layout = spmv.LAYOUT_BY_NAME[name]
@@ -541,25 +554,20 @@ def chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threa
             continue
         op = spmv.Operator(shard, layout, dtype, tpr, device=local_rank)
         info = op.info()
-        # one chained product from x0, its rows checked against the oracle on a block of this rank's rows and
-        # on the first rows of the next rank's shard (rows that reached this rank through its peers' stores);
-        # checked on the first product because the matrix is diagonally dominant: x grows by about 64 each
-        # product and overflows FP32 within the timed products
+        # two chained products from x0, a block of this rank's rows checked bit for bit against the oracle
+        # (checked this early because the matrix is diagonally dominant: x grows by about 64 each product
+        # and overflows FP32 within the timed products)
         group.write_x(x_host.ctypes.data, x_host.nbytes)
         ranks.barrier()
-        spmv.chain_run_peer(op, group, bounds, 1, stream.cuda_stream, timeout_ms=60000)
+        spmv.chain_run_peer(op, group, bounds, 2, stream.cuda_stream, timeout_ms=60000)
         group.check()
         x_after = np.empty_like(x_host)
         group.read_x(x_after.ctypes.data, x_after.nbytes)
-        mismatched, max_abs = oracle_mismatches(s_ptr, s_col, s_val, x_host, x_after[first:first + sample_rows],
-                                                dtype, tpr, threads)
-        if world > 1:
-            peer_first = int(bounds[(rank + 1) % world])
-            mismatched_peer, max_peer = oracle_mismatches(p_ptr, p_col, p_val, x_host,
-                                                          x_after[peer_first:peer_first + peer_rows], dtype, tpr,
-                                                          threads)
-            mismatched += mismatched_peer
-            max_abs = max(max_abs, max_peer)
+        got = x_after[first:first + sample_rows]
+        mismatched = int(np.count_nonzero(got.view(np.uint32) != x_second_block.view(np.uint32)))
+        delta = np.abs(got.astype(np.float64) - x_second_block.astype(np.float64))
+        delta = delta[np.isfinite(delta)]
+        max_abs = float(delta.max()) if delta.size else 0.0
         ranks.barrier()
         spmv.chain_run_peer(op, group, bounds, args.warmup, stream.cuda_stream, timeout_ms=60000)
         group.check()
@@ -573,7 +581,7 @@ def chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threa
         group.check()
         chain_ms = start.elapsed_time(end)
         ranks.barrier()
-        # the product kernels alone on this rank's rows, x held still (no stores to peers, no barrier)
+        # the product kernels alone on this rank's rows, x held still (no exchange, no barrier)
         x_now = group.x(0)
         kernel_ms = event_ms(torch, stream, lambda: op.run(x_now, y_alone.data_ptr(), stream.cuda_stream),
                              args.steps) / args.steps
@@ -589,17 +597,23 @@ def chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threa
             "kernel_gbs_per_rank": round(bytes_per_rank / (kernel_ms * 1e-3) / 1e9, 1),
             "kernel_frac_per_rank": round(bytes_per_rank / (kernel_ms * 1e-3) / 1e9 / peak, 4),
             "physical_tpr": info.physical_tpr, "tile_nnz": info.tile_nnz,
-            "gpu_launches_per_step": 2,
-            "parity": {"checked": True, "rows_per_rank": sample_rows + (peer_rows if world > 1 else 0),
-                       "mismatched_rows": int(mismatched), "max_abs_diff": max_abs, "bit_identical": mismatched == 0,
-                       "against": f"oracle reference-order CSR-i32 product at T={tpr} of x0, on the first chained "
-                                  "product: a block of each rank's own rows and, at N > 1, of the next rank's rows "
-                                  "as they arrived through peer memory"}}
+            "gpu_launches_per_step": 3 if args.chain_exchange == "halo" and world > 1 else 2,
+            "parity": {"checked": True, "rows_per_rank": sample_rows, "mismatched_rows": int(mismatched),
+                       "max_abs_diff": max_abs, "bit_identical": mismatched == 0,
+                       "against": f"oracle reference-order CSR-i32 products at T={tpr}: the second chained product "
+                                  "from x0 on the first rows of each rank's shard, whose columns reach into the "
+                                  "previous rank's rows"}}
         op.close()
     ranks.barrier()
     group.close()
     out["setup_s"] = round(time.time() - started, 1)
     return out
+
+
+def oracle_product(row_ptr, col_ind, values, x, dtype_code, tpr, threads):
+    """The oracle's reference-order CSR-i32 product at T (the checker of the chained products)."""
+    oracle = oracle_module(threads)
+    return oracle.spmv_csr(row_ptr, col_ind, values, x, dtype_code, oracle.I32, tpr, threads=threads)
 
 
 def sweep(args, torch, spmv, stencil, dtype_code, torch_dtype, stream):

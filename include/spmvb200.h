@@ -422,6 +422,14 @@ int spmv_peer_group_barrier(spmv_peer_group* group, int timeout_ms, void* stream
 /* Synchronises the device and reads the group's status word: SPMV_ERR_TIMEOUT if a barrier gave up (the
  * group then refuses further runs; its buffers are undefined). */
 int spmv_peer_group_check(spmv_peer_group* group);
+/* Halo mode for this rank's row shard (the spmv_csr of its rows, cols = n): lists the entries of x that other
+ * ranks own and these rows read (runs split per owner). Chained products then store nothing into the
+ * peers; after each product's barrier this rank pulls just those entries of the next x from their
+ * owners' memory. Each rank's x buffers then hold its own rows and the entries its rows read; the other
+ * entries are not kept up to date. Call before the first spmv_chain_run_peer of this shard. */
+int spmv_peer_group_set_halo(spmv_peer_group* group, const spmv_csr* shard, const int* shard_row_begin);
+/* The number of x entries the halo pulls each product (-1 when no halo is set). */
+int spmv_peer_group_halo_entries(const spmv_peer_group* group, int64_t* entries);
 /* products chained products y -> x over the row shards (shard_row_begin[0..nranks], the rank's operator
  * holding rows shard_row_begin[rank] .. shard_row_begin[rank+1] of the square matrix): one barrier, then
  * per product the fused product and a barrier. The current x advances by products. */

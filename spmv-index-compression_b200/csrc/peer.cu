@@ -16,6 +16,13 @@
 // before every rank has stored into it, and no rank stores into a buffer another rank still reads (the
 // next product's stores go to the other buffer, which every rank finished reading before the barrier).
 //
+// Halo mode (spmv_peer_group_set_halo): a rank's rows usually read few of the other ranks' entries of x (a
+// block FEM matrix, rows coupled within +-50,000: about 100,000 entries of 4 M a rank). After the set-up
+// lists those entries (runs, split into chunks per owner), a chained product stores nothing into the peers;
+// after the barrier one small kernel pulls the listed entries of the next x from their owners' memory
+// (peer loads over NVLink) into this rank's next x. Each rank's x then holds its own rows and the entries
+// its rows read; the others are not kept up to date.
+//
 // No counterpart in the reference (its benchmark runs on one GPU); the per-row results are the
 // single-GPU operator's, so chained results are bit-identical to the oracle's chain.
 #include <cuda_runtime.h>
@@ -23,6 +30,7 @@
 #include <cstring>
 #include <memory>
 #include <string>
+#include <vector>
 
 #include "capi_internal.hpp"
 #include "kernels.cuh"
@@ -65,6 +73,9 @@ __device__ __forceinline__ unsigned long long load_acquire_system(const unsigned
 __global__ void __launch_bounds__(32) k_peer_barrier(const BarrierArgs a) {
   const int t = threadIdx.x;
   if (t >= a.nranks) return;
+  // this rank's earlier kernels' stores (its rows of the next x, into its own memory and its peers') are
+  // visible at system scope before any rank can see the flag
+  __threadfence_system();
   if (a.flags[t]) store_release_system(a.flags[t] + a.rank, a.epoch);
   const uint64_t start = global_timer_ns();
   for (uint32_t spin = 0; spin < (1u << 24); ++spin) {
@@ -73,6 +84,37 @@ __global__ void __launch_bounds__(32) k_peer_barrier(const BarrierArgs a) {
     __nanosleep(256);
   }
   atomicOr(a.status, kStatusTimeout);
+}
+
+// A chunk of the halo: x entries [begin, end) owned by rank `owner`, at most kHaloChunk of them.
+constexpr int kHaloChunk = 2048;
+struct HaloArgs {
+  const int4* chunks;                  // {begin, end, owner, 0}
+  int chunk_count;
+  const char* sources[kMaxRanks];      // every rank's next x as mapped here
+  char* target;                        // this rank's next x
+  int value_bytes;
+};
+
+// Block b copies chunk b of the halo from its owner's next x into this rank's next x. The loads read another
+// GPU's memory that this kernel's rank saw published by the barrier: they bypass the caches (ld.global.cv),
+// so that no copy from before the barrier is read.
+__global__ void __launch_bounds__(256) k_halo_pull(const HaloArgs a) {
+  const int4 chunk = a.chunks[blockIdx.x];
+  const char* source = a.sources[chunk.z];
+  if (a.value_bytes == 8) {
+    const unsigned long long* from = reinterpret_cast<const unsigned long long*>(source);
+    unsigned long long* to = reinterpret_cast<unsigned long long*>(a.target);
+    for (int i = chunk.x + (int)threadIdx.x; i < chunk.y; i += blockDim.x) to[i] = __ldcv(from + i);
+  } else if (a.value_bytes == 4) {
+    const unsigned* from = reinterpret_cast<const unsigned*>(source);
+    unsigned* to = reinterpret_cast<unsigned*>(a.target);
+    for (int i = chunk.x + (int)threadIdx.x; i < chunk.y; i += blockDim.x) to[i] = __ldcv(from + i);
+  } else {
+    const unsigned short* from = reinterpret_cast<const unsigned short*>(source);
+    unsigned short* to = reinterpret_cast<unsigned short*>(a.target);
+    for (int i = chunk.x + (int)threadIdx.x; i < chunk.y; i += blockDim.x) to[i] = __ldcv(from + i);
+  }
 }
 
 }  // namespace
@@ -90,6 +132,13 @@ struct spmv_peer_group {
   bool failed = false;
   int current = 0;                       // the buffer holding the current x (the next product's input)
   unsigned long long epoch = 0;
+  // halo mode (spmv_peer_group_set_halo): the x entries other ranks own that this rank's rows read, as
+  // chunks {begin, end, owner} on the device; pulled from their owners after each product's barrier
+  int4* halo = nullptr;
+  int halo_chunks = 0;
+  bool halo_set = false;
+  int64_t halo_entries = 0;
+  int halo_rows_begin = 0, halo_rows_end = 0;   // the row shard the halo was planned for
 
   char* x_buffer(int rank_of, int which) const { return mapped[rank_of] + (size_t)which * pitch; }
   unsigned long long* flags(int rank_of) const {
@@ -104,6 +153,7 @@ struct spmv_peer_group {
     for (int r = 0; r < nranks; ++r)
       if (r != rank && mapped[r]) cudaIpcCloseMemHandle(mapped[r]);
     if (local) cudaFree(local);
+    if (halo) cudaFree(halo);
     if (previous >= 0 && previous != device) cudaSetDevice(previous);
   }
 };
@@ -228,6 +278,64 @@ int spmv_peer_group_check(spmv_peer_group* group) {
   return status != SPMV_OK ? status : (timed_out ? SPMV_ERR_TIMEOUT : SPMV_OK);
 }
 
+int spmv_peer_group_set_halo(spmv_peer_group* group, const spmv_csr* shard, const int* shard_row_begin) {
+  return guarded([&] {
+    require(group && shard && shard_row_begin, "group, shard and shard_row_begin are required");
+    const Csr& m = shard->m;
+    const int nranks = group->nranks, rank = group->rank;
+    const int64_t n = shard_row_begin[nranks];
+    require(shard_row_begin[0] == 0 && shard_row_begin[rank + 1] - shard_row_begin[rank] == m.rows && m.cols == n,
+            "the shard's rows or columns do not match shard_row_begin");
+    const int own_begin = shard_row_begin[rank], own_end = shard_row_begin[rank + 1];
+    // the columns outside this rank's rows that its rows read
+    std::vector<unsigned char> read((size_t)n, 0);   // set by several host threads: relaxed atomic stores
+    parallel_for(m.rows, [&](int64_t first, int64_t last) {
+      for (int64_t row = first; row < last; ++row)
+        for (int entry = m.row_ptr[row]; entry < m.row_ptr[row + 1]; ++entry) {
+          const int column = m.col_ind[entry];
+          if (column < own_begin || column >= own_end) __atomic_store_n(&read[(size_t)column], 1, __ATOMIC_RELAXED);
+        }
+    });
+    // runs of them (gaps of up to 32 entries bridged), split at the owners' bounds and into chunks
+    std::vector<int4> chunks;
+    int64_t entries = 0;
+    int owner = 0;
+    for (int64_t column = 0; column < n;) {
+      if (!read[(size_t)column]) { ++column; continue; }
+      while (shard_row_begin[owner + 1] <= column) ++owner;
+      int64_t end = column + 1, last_read = column;
+      while (end < shard_row_begin[owner + 1] && end - last_read <= 32) {
+        if (read[(size_t)end]) last_read = end;
+        ++end;
+      }
+      for (int64_t begin = column; begin <= last_read; begin += kHaloChunk)
+        chunks.push_back(make_int4((int)begin, (int)std::min<int64_t>(begin + kHaloChunk, last_read + 1), owner, 0));
+      entries += last_read + 1 - column;
+      column = last_read + 1;
+    }
+    require(chunks.size() < 0x7fffffff, "halo too large");
+    DeviceScope scope(group->device);
+    if (group->halo) cudaFree(group->halo);
+    group->halo = nullptr;
+    if (!chunks.empty()) {
+      cuda_ok(cudaMalloc(reinterpret_cast<void**>(&group->halo), sizeof(int4) * chunks.size()), "cudaMalloc");
+      cuda_ok(cudaMemcpy(group->halo, chunks.data(), sizeof(int4) * chunks.size(), cudaMemcpyHostToDevice), "halo upload");
+    }
+    group->halo_chunks = (int)chunks.size();
+    group->halo_entries = entries;
+    group->halo_rows_begin = own_begin;
+    group->halo_rows_end = own_end;
+    group->halo_set = true;
+  });
+}
+
+int spmv_peer_group_halo_entries(const spmv_peer_group* group, int64_t* entries) {
+  return guarded([&] {
+    require(group && entries, "group and entries are required");
+    *entries = group->halo_set ? group->halo_entries : -1;
+  });
+}
+
 int spmv_chain_run_peer(const spmv_operator* shard_op, spmv_peer_group* group, const int* shard_row_begin, int products,
                         int timeout_ms, void* stream) {
   return guarded([&] {
@@ -249,16 +357,30 @@ int spmv_chain_run_peer(const spmv_operator* shard_op, spmv_peer_group* group, c
     const size_t offset = value_bytes * (size_t)shard_row_begin[rank];
     // every rank has reached this point in its stream before any stores into its buffers
     launch_barrier(group, timeout_ms, s);
+    if (group->halo_set)
+      require(group->halo_rows_begin == shard_row_begin[rank] && group->halo_rows_end == shard_row_begin[rank + 1],
+              "the halo was planned for another row shard");
     for (int product = 0; product < products; ++product) {
       const int next = 1 - group->current;
       void* peers[kMaxPeers];
       int count = 0;
-      for (int r = 0; r < nranks; ++r)
-        if (r != rank) peers[count++] = group->x_buffer(r, next) + offset;
+      if (!group->halo_set)   // every row stored into every rank's next x as well
+        for (int r = 0; r < nranks; ++r)
+          if (r != rank) peers[count++] = group->x_buffer(r, next) + offset;
       cuda_ok(run_operator_with_peers(shard_op, group->x_buffer(rank, group->current), group->x_buffer(rank, next) + offset,
                                       peers, count, s),
               "chained product");
       launch_barrier(group, timeout_ms, s);
+      if (group->halo_set && group->halo_chunks > 0) {   // the entries of the next x this rank's rows read
+        HaloArgs h{};
+        h.chunks = group->halo;
+        h.chunk_count = group->halo_chunks;
+        for (int r = 0; r < nranks; ++r) h.sources[r] = group->x_buffer(r, next);
+        h.target = group->x_buffer(rank, next);
+        h.value_bytes = (int)value_bytes;
+        k_halo_pull<<<(unsigned)group->halo_chunks, 256, 0, s>>>(h);
+        cuda_ok(cudaGetLastError(), "halo pull");
+      }
       group->current = next;
     }
   });

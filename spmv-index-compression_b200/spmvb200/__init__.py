@@ -199,6 +199,8 @@ _sig("spmv_peer_group_barrier", _i, _v, _i, _v)
 _sig("spmv_peer_group_copy_x", _i, _v, _i, _v, _i64, _v)
 _sig("spmv_peer_group_check", _i, _v)
 _sig("spmv_chain_run_peer", _i, _v, _v, _v, _i, _i, _v)
+_sig("spmv_peer_group_set_halo", _i, _v, _v, _v)
+_sig("spmv_peer_group_halo_entries", _i, _v, ctypes.POINTER(_i64))
 _sig("spmv_peer_group_destroy", None, _v)
 
 
@@ -749,6 +751,15 @@ class PeerGroup:
     def read_x(self, pointer: int, nbytes: int, stream: int = 0):
         """Copies nbytes of this rank's current x to pointer (host or device memory)."""
         _check(_lib.spmv_peer_group_copy_x(self._handle, 1, pointer, nbytes, stream or None))
+
+    def set_halo(self, shard: "CsrMatrix", shard_row_begin):
+        """Halo mode for this rank's row shard: each chained product pulls only the entries of x that other
+        ranks own and these rows read. Returns the number of entries pulled per product."""
+        bounds = np.ascontiguousarray(shard_row_begin, dtype=np.int32)
+        _check(_lib.spmv_peer_group_set_halo(self._handle, shard.handle, _pointer(bounds)))
+        count = ctypes.c_int64()
+        _check(_lib.spmv_peer_group_halo_entries(self._handle, ctypes.byref(count)))
+        return count.value
 
     def barrier(self, timeout_ms: int = 5000, stream: int = 0):
         _check(_lib.spmv_peer_group_barrier(self._handle, timeout_ms, stream or None))

@@ -3,7 +3,8 @@ slice of the next x, the slices all-gathered (grouped broadcasts for nnz-balance
 one all-gather for equal ones), three times; and over interleaved row blocks whose all-gathers run beside
 the next block's product (spmv_chain_run_blocks); and over peer memory, each product storing its rows into
 both GPUs' next x (spmv_chain_run_peer); the results bit-identical to the oracle's chain on the whole
-matrix."""
+matrix; and in halo mode, each product pulling only the entries of x the rank's rows read from the other
+GPU."""
 import datetime
 import os
 import socket
@@ -89,6 +90,24 @@ def worker(rank, world, port):
                 result = np.empty_like(x0)
                 group.read_x(result.ctypes.data, result.nbytes)
                 assert np.array_equal(result.view(np.uint64), want.view(np.uint64)), (bounds.tolist(), products)
+        dist.barrier()
+    # halo mode: each product pulls only the entries of x the rank's rows read from the other rank; each
+    # rank's own rows of the chain are the oracle's, and the halo is a small part of x
+    for bounds in (spmv.shard_rows(matrix, world), np.array([0, 10000, 20000], dtype=np.int32)):
+        first, last = int(bounds[rank]), int(bounds[rank + 1])
+        shard = matrix.slice_rows(first, last)
+        halo = group.set_halo(shard, bounds)
+        assert 0 < halo < matrix.cols // 4, halo
+        with spmv.Operator(shard, spmv.LP, spmv.F64, 8, device=rank) as op:
+            group.write_x(x0.ctypes.data, x0.nbytes)
+            dist.barrier()
+            for products, want in ((3, expected), (1, fourth)):
+                spmv.chain_run_peer(op, group, bounds, products, stream, timeout_ms=20000)
+                group.check()
+                result = np.empty_like(x0)
+                group.read_x(result.ctypes.data, result.nbytes)
+                assert np.array_equal(result[first:last].view(np.uint64), want[first:last].view(np.uint64)), \
+                    ("halo", bounds.tolist(), products)
         dist.barrier()
     group.close()
     comm.close()
