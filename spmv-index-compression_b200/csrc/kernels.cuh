@@ -1105,7 +1105,9 @@ __device__ __forceinline__ void listed_rows(const KernelArgs& a, int segment, in
   const bool active = index < a.segment_items[segment];
   const int4 item = active ? __ldg(a.row_items + a.segment_first[segment] + index) : make_int4(0, 0, 0, 0);
   const GlobalView<V, LAYOUT> g(a);
-  constexpr int kBatch = ClassGathers<V>::value;
+  // CSR-lp gathers half as deep: its decode state and the 16-deep batch spill at the class kernel's 64
+  // registers (44 bytes a thread for FP16 at T = 32)
+  constexpr int kBatch = LAYOUT == SPMV_LAYOUT_LP ? ClassGathers<V>::value / 2 : ClassGathers<V>::value;
   if constexpr (LAYOUT == SPMV_LAYOUT_LP) {
     // CSR-lp: lane by lane (one running column), all of a row's gathers at once when it has at most R
     // rounds, else four deltas of a lane at a time
