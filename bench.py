@@ -75,7 +75,8 @@ def parse_args():
     parser.add_argument("--chain-exchange", choices=("halo", "push"), default="halo",
                         help="chained: each product pulls only the entries of x its rows read from the other ranks "
                              "(halo), or stores its rows into every rank's next x (push)")
-    parser.add_argument("--no-sweep", action="store_true", help="skip the per-layout/T table and comparators")
+    parser.add_argument("--no-sweep", action="store_true",
+                        help="skip the per-layout/T table and comparators (one GPU) or the sharded power-law leg (N GPUs)")
     parser.add_argument("--no-chained", action="store_true", help="skip the chained block-FEM products")
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget")
     return parser.parse_args()
@@ -453,6 +454,8 @@ def run_ours(args, rank, world, local_rank):
         del x, y
         op.close()
         chained = chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threads)
+    if world > 1 and not args.no_sweep:
+        extras["sharded_powerlaw"] = sharded_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threads)
     if world == 1 and not args.no_sweep:
         extras = sweep(args, torch, spmv, matrix, dtype_code, torch_dtype, stream)
         rate, sample, cores = cpu_product_rate(matrix, dtype_code, args.tpr, args.cpu_seconds)
@@ -614,6 +617,43 @@ def chained_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threa
     return out
 
 
+def sharded_leg(args, torch, spmv, ranks, rank, world, local_rank, stream, threads):
+    """Config 4 at N GPUs: the power-law matrix (n = 8M, FP16) in nnz-balanced row shards, x replicated, CSR-i32
+    and CSR-lp at T = 32 (rows by length); the product of every rank timed with the reference's protocol, max
+    over ranks; each rank's rows checked bit for bit against the oracle."""
+    matrix = build_matrix(spmv, "powerlaw")
+    dtype = spmv.DTYPE_BY_NAME["fp16"]
+    bounds = spmv.shard_rows(matrix, world)
+    first, last = int(bounds[rank]), int(bounds[rank + 1])
+    shard = matrix.slice_rows(first, last)
+    x_host = spmv.fill_uniform(dtype, matrix.cols, SEED_OF["powerlaw"])
+    x = torch.from_numpy(x_host).to(f"cuda:{local_rank}")
+    y = torch.empty(shard.rows, dtype=torch.float16, device=f"cuda:{local_rank}")
+    s_ptr, s_col, s_val = shard.arrays()
+    out = {"workload": WORKLOADS["powerlaw"], "rows": matrix.rows, "nnz": matrix.nnz, "tpr": 32, "n_gpus": world,
+           "parallelism": f"row shards x{world} (nnz-balanced, x replicated)", "layouts": {}}
+    facts = spmv.facts_of(shard)
+    for name in ("i32", "lp"):
+        layout = spmv.LAYOUT_BY_NAME[name]
+        if not spmv.configuration_admissible(shard, facts, spmv.Configuration.of(layout, dtype, 32)):
+            out["layouts"][name] = {"status": "not admissible"}
+            continue
+        with spmv.Operator(shard, layout, dtype, 32, device=local_rank) as op:
+            body = lambda: op.run(x.data_ptr(), y.data_ptr(), stream.cuda_stream)  # noqa: E731
+            ranks.barrier()
+            ms, batch = protocol_median_ms(torch, stream, body)
+            body()
+            torch.cuda.synchronize()
+            op.check()
+        mismatched, max_abs = oracle_mismatches(s_ptr, s_col, s_val, x_host, y.cpu().numpy(), dtype, 32, threads)
+        ms, max_abs = ranks.max([ms, max_abs])
+        (mismatched,) = ranks.sum([mismatched])
+        out["layouts"][name] = {"status": "ok", "t_ms": round(ms, 6), "gflops": round(2.0 * matrix.nnz / (ms * 1e-3) / 1e9, 2),
+                                "parity": {"checked": True, "rows": matrix.rows, "mismatched_rows": int(mismatched),
+                                           "max_abs_diff": max_abs, "bit_identical": mismatched == 0}}
+    return out
+
+
 def oracle_product(row_ptr, col_ind, values, x, dtype_code, tpr, threads):
     """The oracle's reference-order CSR-i32 product at T (the checker of the chained products)."""
     oracle = oracle_module(threads)
@@ -656,6 +696,9 @@ def sweep(args, torch, spmv, stencil, dtype_code, torch_dtype, stream):
                     if workload == "stencil27" and name in ("i32", "lp"):
                         comparators.setdefault("reference_sm100a", []).append(
                             reference_kernels(torch, spmv, op, matrix, dtype, layout, tpr, x, y, ms))
+                    if workload == "band" and name == "r16":
+                        comparators.setdefault("r16_controls", []).extend(
+                            r16_controls(torch, spmv, op, matrix, dtype, tpr, x, ms, i32_bits, bits_type))
                 bits = y.view(bits_type).clone()
                 if name == "i32":
                     i32_ms, i32_bits = ms, bits
@@ -695,6 +738,36 @@ def cusparse_comparator(torch, spmv, matrix, facts, dtype, tdtype, x, stream):
             return out
     except Exception as failure:  # the comparator is optional
         return {"error": str(failure)[:200]}
+
+
+def r16_controls(torch, spmv, op, matrix, dtype, tpr, x, library_ms, i32_bits, bits_type):
+    """The reference's control builds of CSR-r16 (bench_csr_width.cu:34-42: lane-major offsets, the same two to
+    a 32-bit load, 32-bit offsets, the loop unrolled 16 times) launched on the r16 operator's arrays, each timed
+    with the reference's protocol and its y compared bit for bit with CSR-i32's at the same T."""
+    out = []
+    arrays = op.arrays()
+    lane = torch.from_numpy(spmv.encode_relative_lane(matrix, tpr).view(np.int16)).cuda()
+    wide = torch.from_numpy(spmv.encode_relative(matrix, 4).view(np.int32)).cuda()
+    facts = spmv.facts_of(matrix)
+    base = spmv.memory_of(matrix, facts, spmv.Configuration.of(spmv.R16, dtype, tpr)).total
+    for name, control in spmv.R16_CONTROLS.items():
+        offsets = {"lane": lane, "pair": lane, "wide": wide}.get(name)
+        y = torch.empty(matrix.rows, dtype=x.dtype, device="cuda")
+        device = spmv.DeviceMatrix(rows=matrix.rows, cols=matrix.cols, nnz=matrix.nnz, row_ptr=arrays.row_ptr,
+                                   columns=offsets.data_ptr() if offsets is not None else arrays.columns,
+                                   row_base=arrays.row_base, values=arrays.values, x=x.data_ptr(), y=y.data_ptr())
+        body = lambda: spmv.launch_r16_control(control, dtype, tpr, device, torch.cuda.current_stream().cuda_stream)  # noqa: E731
+        ms, batch = protocol_median_ms(torch, torch.cuda.current_stream(), body)
+        body()
+        torch.cuda.synchronize()
+        total = base + (2 * matrix.nnz if name == "wide" else 0)
+        out.append({"control": name, "tpr": tpr, "t_ms": round(ms, 6), "batch": batch,
+                    "gflops": round(2.0 * matrix.nnz / (ms * 1e-3) / 1e9, 2), "bytes": total,
+                    "library_r16_t_ms": round(library_ms, 6), "library_speedup": round(ms / library_ms, 4),
+                    "bits_equal_i32": bool(torch.equal(y.view(bits_type), i32_bits)) if i32_bits is not None else None})
+        del y
+    del lane, wide
+    return out
 
 
 def reference_kernels(torch, spmv, op, matrix, dtype, layout, tpr, x, y, library_ms):

@@ -170,6 +170,10 @@ int spmv_encode_absolute(const spmv_csr* matrix, int column_bytes, void* columns
 int spmv_encode_row_base(const spmv_csr* matrix, int* row_base);
 /* upload_relative_columns<I> (bench_csr_width.cu:820): col - row base in 2 (r16) or 1 (r8) bytes. */
 int spmv_encode_relative(const spmv_csr* matrix, int column_bytes, void* offsets);
+/* upload_lane_major_offsets (bench_csr_width.cu:838, control builds SPMV_R16_LANE/PAIR): the 16-bit
+ * row-relative offsets of every row in lane-major order for tpr, (nnz + 1) / 2 * 2 entries (the last one zero
+ * when nnz is odd). column_bytes 4 in spmv_encode_relative gives SPMV_R16_WIDE's 32-bit offsets (:944). */
+int spmv_encode_relative_lane(const spmv_csr* matrix, int tpr, uint16_t* offsets);
 /* packed_word_count (bench_csr_width.cu:206). */
 int spmv_lane_packed_word_count(const spmv_csr* matrix, int tpr, int64_t* word_count);
 /* build_packed_deltas (bench_csr_width.cu:861): row_word[rows], row_width[rows], words[word_count]. */
@@ -305,6 +309,15 @@ typedef struct {
 /* launch<T> (bench_csr_width.cu:607-629) on caller arrays: one vector of T threads per row, no
  * preprocessing and no workspace. */
 int spmv_launch(int layout, int dtype, int tpr, const spmv_device_matrix* matrix, void* stream);
+
+/* The reference's CSR-r16 control builds (bench_csr_width.cu:34-42, :343-432, CMakeLists.txt:36-47), each
+ * changing only how the offsets reach its global-memory r16 kernel, on caller arrays like spmv_launch:
+ * LANE reads matrix->columns as the lane-major stream for tpr (spmv_encode_relative_lane), PAIR the same
+ * stream two offsets to a 32-bit load (4-byte aligned), WIDE as 32-bit offsets (spmv_encode_relative with
+ * column_bytes 4), UNROLL16 as the 16-bit offsets with the loop unrolled 16 times at FP16. row_ptr,
+ * row_base, values, x and y as for CSR-r16. The results are CSR-i32's bits at the same tpr. */
+enum { SPMV_R16_CONTROL_LANE = 1, SPMV_R16_CONTROL_PAIR = 2, SPMV_R16_CONTROL_WIDE = 3, SPMV_R16_CONTROL_UNROLL16 = 4 };
+int spmv_launch_r16_control(int control, int dtype, int tpr, const spmv_device_matrix* matrix, void* stream);
 
 /* measure_read_bandwidth (include/roofline.cuh:101): the median bandwidth of a pure streaming read of a
  * `bytes`-byte device buffer (16-byte vector loads, no reuse), over `reps` timed passes after 3 warm-ups,

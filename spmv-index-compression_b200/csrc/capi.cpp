@@ -289,6 +289,14 @@ int spmv_encode_relative(const spmv_csr* matrix, int column_bytes, void* offsets
   });
 }
 
+int spmv_encode_relative_lane(const spmv_csr* matrix, int tpr, uint16_t* offsets) {
+  return guarded([&] {
+    require(matrix && offsets, "matrix and offsets are required");
+    require(valid_tpr(tpr), "threads per row must be 2, 4, 8, 16 or 32");
+    encode_relative_lane(matrix->m, tpr, offsets);
+  });
+}
+
 int spmv_lane_packed_word_count(const spmv_csr* matrix, int tpr, int64_t* word_count) {
   return guarded([&] {
     require(matrix && word_count, "matrix and word_count are required");

@@ -89,6 +89,7 @@ int column_bytes_of(int layout);
 void encode_absolute(const Csr& matrix, int column_bytes, void* out);
 void encode_row_base(const Csr& matrix, int* row_base);
 void encode_relative(const Csr& matrix, int column_bytes, void* out);
+void encode_relative_lane(const Csr& matrix, int tpr, uint16_t* out);
 void encode_lane_packed(const Csr& matrix, int tpr, int64_t word_count, int* row_word, uint8_t* row_width,
                         uint32_t* words);
 

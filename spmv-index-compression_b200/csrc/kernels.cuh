@@ -92,6 +92,10 @@ template <> struct LayoutTraits<SPMV_LAYOUT_I8>  { using Index = uint8_t;  stati
 template <> struct LayoutTraits<SPMV_LAYOUT_R16> { using Index = uint16_t; static constexpr bool kBase = true; };
 template <> struct LayoutTraits<SPMV_LAYOUT_R8>  { using Index = uint8_t;  static constexpr bool kBase = true; };
 template <> struct LayoutTraits<SPMV_LAYOUT_LP>  { using Index = uint32_t; static constexpr bool kBase = true; };
+// Row-relative offsets in 32 bits: the CSR-r16 control build SPMV_R16_WIDE (bench_csr_width.cu:38-39, :944),
+// raw launch only.
+constexpr int kLayoutR16Wide = 100;
+template <> struct LayoutTraits<kLayoutR16Wide> { using Index = uint32_t; static constexpr bool kBase = true; };
 
 // Arguments of every kernel (device pointers).
 struct KernelArgs {
@@ -448,7 +452,7 @@ __device__ __forceinline__ uint32_t packed_delta(const View& view, int64_t w0, B
 // ---- the vector path -----------------------------------------------------------------------------------
 // One group of T threads per row, each thread one logical lane, straight from global memory. CTA `block`
 // of `blocks` (of BLOCK threads each) takes the rows item = group, group + groups, ... of the row list.
-template <class V, int LAYOUT, int T, int BLOCK>
+template <class V, int LAYOUT, int T, int BLOCK, int UNROLL = 4>
 __device__ __forceinline__ void vector_rows(const KernelArgs& a, int64_t block, int64_t blocks) {
   using VT = ValueTraits<V>;
   using Acc = typename VT::Acc;
@@ -471,7 +475,7 @@ __device__ __forceinline__ void vector_rows(const KernelArgs& a, int64_t block, 
       if constexpr (!kPacked) {
         const Index* columns = static_cast<const Index*>(a.columns);
         const int base = kBase ? a.row_base[row] : 0;
-#pragma unroll 4
+#pragma unroll UNROLL
         for (int64_t entry = entry_begin + lane; entry < entry_end; entry += T)
           sum = VT::fma(VT::widen(load_readonly(values + entry)),
                         VT::widen(load_readonly(x + base + (int)load_readonly(columns + entry))), sum);

@@ -140,14 +140,38 @@ void encode_row_base(const Csr& matrix, int* row_base) {
 }
 
 void encode_relative(const Csr& matrix, int column_bytes, void* out) {
-  if (column_bytes != 1 && column_bytes != 2) fail(SPMV_ERR_INVALID_ARGUMENT, "column_bytes must be 1 or 2");
+  if (column_bytes != 1 && column_bytes != 2 && column_bytes != 4)
+    fail(SPMV_ERR_INVALID_ARGUMENT, "column_bytes must be 1, 2 or 4");
   parallel_for(matrix.rows, [&](int64_t first, int64_t last) {
     for (int64_t row = first; row < last; ++row) {
       const int begin = matrix.row_ptr[row], end = matrix.row_ptr[row + 1];
       const int base = end > begin ? matrix.col_ind[begin] : 0;
       for (int entry = begin; entry < end; ++entry) {
-        if (column_bytes == 2) static_cast<uint16_t*>(out)[entry] = (uint16_t)(matrix.col_ind[entry] - base);
-        else                   static_cast<uint8_t*>(out)[entry] = (uint8_t)(matrix.col_ind[entry] - base);
+        if (column_bytes == 4)      static_cast<uint32_t*>(out)[entry] = (uint32_t)(matrix.col_ind[entry] - base);
+        else if (column_bytes == 2) static_cast<uint16_t*>(out)[entry] = (uint16_t)(matrix.col_ind[entry] - base);
+        else                        static_cast<uint8_t*>(out)[entry] = (uint8_t)(matrix.col_ind[entry] - base);
+      }
+    }
+  }, 4096);
+}
+
+// The 16-bit row-relative offsets of every row in lane-major order for T (upload_lane_major_offsets,
+// bench_csr_width.cu:838): within the row's own positions, logical lane L's offsets (entries L, L+T, ...)
+// come next to each other from position L * quotient + min(L, remainder); (nnz + 1) / 2 * 2 entries, the last
+// one zero when nnz is odd, so that 32-bit loads of two offsets never read past the stream.
+void encode_relative_lane(const Csr& matrix, int tpr, uint16_t* out) {
+  const int64_t count = (matrix.nnz() + 1) / 2 * 2;
+  if (count > matrix.nnz()) out[count - 1] = 0;
+  parallel_for(matrix.rows, [&](int64_t first, int64_t last) {
+    for (int64_t row = first; row < last; ++row) {
+      const int begin = matrix.row_ptr[row], length = matrix.row_ptr[row + 1] - begin;
+      if (length == 0) continue;
+      const int base = matrix.col_ind[begin];
+      const int quotient = length / tpr, remainder = length - quotient * tpr;
+      for (int lane = 0; lane < tpr && lane < length; ++lane) {
+        int position = begin + lane * quotient + std::min(lane, remainder);
+        for (int entry = begin + lane; entry < begin + length; entry += tpr)
+          out[position++] = (uint16_t)(matrix.col_ind[entry] - base);
       }
     }
   }, 4096);

@@ -4,7 +4,7 @@
 //
 //   spmv_bench --matrix A.mtx [--matrix B.mtx ...] [--reps 30] [--warmup 10] [--ordering original|rcm]
 //              [--min-sample-ms 0] [--tpr-csv FILE] [--csv FILE] [--precision all|fp64|fp32|fp16]
-//              [--accumulate wide|half]
+//              [--accumulate wide|half] [--r16-control lane|pair|wide|unroll16]
 //
 // Per matrix and precision: every layout (i32, i16, i8, r16, r8, lp) at every threads per row T; every
 // result checked against CSR-i32 of the same precision at the same T (it must be bit-identical, so
@@ -38,6 +38,7 @@ struct Args {
   std::string precision = "all";
   // "half": FP16 values summed in FP16, FP16 only (the reference's bench_csr_width_fp16acc build)
   std::string accumulate = "wide";
+  std::string r16_control;   // "", lane, pair, wide or unroll16: the reference's control builds of CSR-r16
   int reps = 30;
   int warmup = 10;
   double min_sample_ms = 0.0;
@@ -237,6 +238,15 @@ void run_cusparse(cusparseHandle_t handle, cusparseSpMVAlg_t algorithm, const sp
   cusparseDestroySpMat(matrix);
 }
 
+// The control build of CSR-r16 named by --r16-control (0: none).
+int r16_control_code(const std::string& name) {
+  if (name == "lane") return SPMV_R16_CONTROL_LANE;
+  if (name == "pair") return SPMV_R16_CONTROL_PAIR;
+  if (name == "wide") return SPMV_R16_CONTROL_WIDE;
+  if (name == "unroll16") return SPMV_R16_CONTROL_UNROLL16;
+  return 0;
+}
+
 void run_precision(spmv_csr* matrix, const std::string& name, int dtype, const Args& args, double read_bandwidth,
                    cusparseHandle_t sparse, cudaStream_t stream) {
   spmv_csr_info info;
@@ -304,11 +314,47 @@ void run_precision(spmv_csr* matrix, const std::string& name, int dtype, const A
       check(spmv_operator_create(matrix, &config, &op), "operator");
       spmv_memory memory;
       check(spmv_memory_of(matrix, &facts, layout.code, dtype, tpr, &memory), "memory_of");
-      check(spmv_operator_run(op, v.x, v.y, stream), "run");
+      // a control build of CSR-r16: the control's kernel on the operator's row_ptr, row_base and values and the
+      // control's offsets (bench_csr_width.cu:615-620); WIDE counts 4 bytes an offset (memory_of, :270)
+      const int control = layout.code == SPMV_LAYOUT_R16 ? r16_control_code(args.r16_control) : 0;
+      void* control_offsets = nullptr;
+      spmv_device_matrix device{};
+      if (control) {
+        spmv_operator_arrays arrays;
+        check(spmv_operator_get_arrays(op, &arrays), "arrays");
+        device.rows = info.rows;
+        device.cols = info.cols;
+        device.nnz = info.nnz;
+        device.row_ptr = arrays.row_ptr;
+        device.row_base = arrays.row_base;
+        device.values = arrays.values;
+        device.x = v.x;
+        device.y = v.y;
+        device.columns = arrays.columns;
+        if (control != SPMV_R16_CONTROL_UNROLL16) {
+          const bool wide = control == SPMV_R16_CONTROL_WIDE;
+          const size_t count = wide ? (size_t)info.nnz : (size_t)((info.nnz + 1) / 2 * 2);
+          std::vector<unsigned char> host(std::max<size_t>(count * (wide ? 4 : 2), 4));
+          if (wide) check(spmv_encode_relative(matrix, 4, host.data()), "wide offsets");
+          else check(spmv_encode_relative_lane(matrix, tpr, reinterpret_cast<uint16_t*>(host.data())), "lane offsets");
+          cuda(cudaMalloc(&control_offsets, host.size()), "cudaMalloc offsets");
+          cuda(cudaMemcpy(control_offsets, host.data(), host.size(), cudaMemcpyHostToDevice), "copy offsets");
+          device.columns = control_offsets;
+          if (wide) {
+            memory.total += (double)info.nnz * 2;
+            memory.columns = (double)info.nnz * 4;
+          }
+        }
+      }
+      auto product = [&] {
+        return control ? spmv_launch_r16_control(control, dtype, tpr, &device, stream) : spmv_operator_run(op, v.x, v.y, stream);
+      };
+      check(product(), "run");
       const double diff = max_difference(v.read(stream), i32_at[tpr]);
       int batch = 1;
-      const double ms = median_ms([&] { spmv_operator_run(op, v.x, v.y, stream); }, args, stream, batch);
+      const double ms = median_ms(product, args, stream, batch);
       check(spmv_operator_check(op), "device status");
+      if (control_offsets) cudaFree(control_offsets);
       spmv_operator_destroy(op);
       samples.push_back({tpr, batch, ms, memory.total, diff});
       if (ms < best_ms) { best_ms = ms; best_tpr = tpr; best_batch = batch; }
@@ -384,7 +430,7 @@ Args parse(int argc, char** argv) {
     if (option == "--help" || i + 1 >= argc) {
       std::printf("usage: spmv_bench --matrix A.mtx [--matrix B.mtx ...] [--reps 30] [--warmup 10] "
                   "[--ordering original|rcm] [--min-sample-ms 0] [--tpr-csv FILE] [--csv FILE] "
-                  "[--precision all|fp64|fp32|fp16] [--accumulate wide|half]\n");
+                  "[--precision all|fp64|fp32|fp16] [--accumulate wide|half] [--r16-control lane|pair|wide|unroll16]\n");
       std::exit(option == "--help" ? 0 : 1);
     }
     const std::string value = argv[++i];
@@ -397,6 +443,7 @@ Args parse(int argc, char** argv) {
     else if (option == "--tpr-csv") args.tpr_csv = value;
     else if (option == "--precision") args.precision = value;
     else if (option == "--accumulate") args.accumulate = value;
+    else if (option == "--r16-control") args.r16_control = value;
     else die("unknown option " + option);
   }
   if (args.matrices.empty()) die("at least one --matrix is required");
@@ -404,6 +451,9 @@ Args parse(int argc, char** argv) {
   if (args.precision != "all" && args.precision != "fp64" && args.precision != "fp32" && args.precision != "fp16")
     die("--precision must be all, fp64, fp32 or fp16");
   if (args.accumulate != "wide" && args.accumulate != "half") die("--accumulate must be wide or half");
+  if (!args.r16_control.empty() && r16_control_code(args.r16_control) == 0)
+    die("--r16-control must be lane, pair, wide or unroll16");
+  if (!args.r16_control.empty() && args.accumulate == "half") die("--r16-control runs with --accumulate wide");
   return args;
 }
 

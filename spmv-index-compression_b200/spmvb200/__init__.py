@@ -174,6 +174,8 @@ _sig("spmv_operator_check", _i, _v)
 _sig("spmv_operator_get_arrays", _i, _v, ctypes.POINTER(OperatorArrays))
 _sig("spmv_operator_destroy", None, _v)
 _sig("spmv_launch", _i, _i, _i, _i, ctypes.POINTER(DeviceMatrix), _v)
+_sig("spmv_launch_r16_control", _i, _i, _i, _i, ctypes.POINTER(DeviceMatrix), _v)
+_sig("spmv_encode_relative_lane", _i, _v, _i, _v)
 _sig("spmv_synth_laplacian2d", _i, _i, _c_void_pp)
 _sig("spmv_synth_random_band", _i, _i, _i, _d, _u64, _c_void_pp)
 _sig("spmv_synth_stencil27", _i, _i, _c_void_pp)
@@ -441,10 +443,20 @@ def encode_row_base(matrix: CsrMatrix) -> np.ndarray:
 
 
 def encode_relative(matrix: CsrMatrix, column_bytes: int) -> np.ndarray:
-    """upload_relative_columns<I> (bench_csr_width.cu:820) on the host."""
-    out = np.zeros(max(matrix.nnz, 1), dtype=np.uint16 if column_bytes == 2 else np.uint8)
+    """upload_relative_columns<I> (bench_csr_width.cu:820) on the host; column_bytes 4 gives the 32-bit
+    offsets of the SPMV_R16_WIDE control build."""
+    dtype = {4: np.uint32, 2: np.uint16}.get(column_bytes, np.uint8)
+    out = np.zeros(max(matrix.nnz, 1), dtype=dtype)
     _check(_lib.spmv_encode_relative(matrix.handle, column_bytes, _pointer(out)))
     return out[:matrix.nnz]
+
+
+def encode_relative_lane(matrix: CsrMatrix, tpr: int) -> np.ndarray:
+    """upload_lane_major_offsets (bench_csr_width.cu:838): the 16-bit offsets of every row in lane-major order
+    for tpr, (nnz + 1) // 2 * 2 entries (the SPMV_R16_LANE / SPMV_R16_PAIR control builds)."""
+    out = np.zeros(max((matrix.nnz + 1) // 2 * 2, 2), dtype=np.uint16)
+    _check(_lib.spmv_encode_relative_lane(matrix.handle, tpr, _pointer(out)))
+    return out[:(matrix.nnz + 1) // 2 * 2]
 
 
 def packed_word_count(matrix: CsrMatrix, tpr: int) -> int:
@@ -642,6 +654,18 @@ def gather_rate(elements: int, value_bytes: int, reps: int = 10) -> float:
 def launch(layout: int, dtype: int, tpr: int, device_matrix: DeviceMatrix, stream: int = 0):
     """launch<T> (bench_csr_width.cu:607) on caller-owned device arrays (no preprocessing)."""
     _check(_lib.spmv_launch(layout, dtype, tpr, ctypes.byref(device_matrix), stream or None))
+
+
+R16_CONTROL_LANE, R16_CONTROL_PAIR, R16_CONTROL_WIDE, R16_CONTROL_UNROLL16 = 1, 2, 3, 4
+R16_CONTROLS = {"lane": R16_CONTROL_LANE, "pair": R16_CONTROL_PAIR, "wide": R16_CONTROL_WIDE,
+                "unroll16": R16_CONTROL_UNROLL16}
+
+
+def launch_r16_control(control: int, dtype: int, tpr: int, device_matrix: DeviceMatrix, stream: int = 0):
+    """A control build of the reference's CSR-r16 kernel (bench_csr_width.cu:34-42) on caller arrays:
+    device_matrix.columns is the lane-major stream (LANE, PAIR), the 32-bit offsets (WIDE) or the 16-bit
+    offsets (UNROLL16)."""
+    _check(_lib.spmv_launch_r16_control(control, dtype, tpr, ctypes.byref(device_matrix), stream or None))
 
 
 # ---------------------------------------------------------------------------------------------------

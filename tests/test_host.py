@@ -393,3 +393,23 @@ def test_slice_rows_matches_arrays():
     assert part.cols == matrix.cols
     assert np.array_equal(p_ptr, row_ptr[100:701] - row_ptr[100])
     assert np.array_equal(p_col, col_ind[row_ptr[100]:row_ptr[700]])
+
+
+def test_r16_control_encoders():
+    """The control builds' offset streams (bench_csr_width.cu:838-855, :944): lane L's 16-bit offsets of a row
+    come next to each other from position L * (length // T) + min(L, length % T) of the row's own positions,
+    padded to whole 32-bit words; the WIDE offsets are the r16 offsets in 32 bits."""
+    row_ptr, col_ind, values = random_csr(300, 5000, lambda rng: rng.integers(0, 70), 17, empty_every=9)
+    matrix = spmv.CsrMatrix.from_arrays(300, 5000, row_ptr, col_ind, values)
+    relative = spmv.encode_relative(matrix, 2)
+    assert np.array_equal(spmv.encode_relative(matrix, 4), relative.astype(np.uint32))
+    for tpr in spmv.THREADS_PER_ROW:
+        want = np.zeros((col_ind.size + 1) // 2 * 2, np.uint16)
+        for row in range(300):
+            begin, end = int(row_ptr[row]), int(row_ptr[row + 1])
+            length = end - begin
+            quotient, remainder = divmod(length, tpr)
+            for offset in range(length):
+                lane, k = offset % tpr, offset // tpr
+                want[begin + lane * quotient + min(lane, remainder) + k] = relative[begin + offset]
+        assert np.array_equal(spmv.encode_relative_lane(matrix, tpr), want), tpr

@@ -110,3 +110,28 @@ def test_half_sums_campaign_rows(smoke_matrix_paths, tmp_path):
     for row in rows:
         if row["status"] == "ok":
             assert float(row["max_abs_diff"]) == 0.0, row
+
+
+@pytest.mark.gpu
+def test_r16_control_campaign_rows(smoke_matrix_paths, tmp_path):
+    """--r16-control (the reference's bench_csr_width_r16{lane,pair,wide,unroll16} builds): the r16 rows are the
+    control kernels', still bit-identical to CSR-i32; WIDE counts 4 bytes an offset."""
+    binary = built()
+    name, path = sorted(smoke_matrix_paths.items())[0]
+    local = tmp_path / os.path.basename(path)
+    os.symlink(path, local)
+    bytes_of = {}
+    for control in ("lane", "pair", "wide", "unroll16"):
+        results = tmp_path / f"{control}.csv"
+        done = subprocess.run([binary, "--matrix", str(local), "--reps", "2", "--warmup", "1", "--precision", "fp64",
+                               "--ordering", "rcm", "--r16-control", control, "--csv", str(results)],
+                              capture_output=True, text=True, timeout=900)
+        assert done.returncode == 0, done.stdout[-2000:] + done.stderr[-2000:]
+        rows = [r for r in csv.DictReader(open(results)) if r["kernel"] == "custom" and r["column_mode"] == "row-base"
+                and r["column_bytes"] == "2"]
+        assert len(rows) == 1, control
+        if rows[0]["status"] == "ok":
+            assert float(rows[0]["max_abs_diff"]) == 0.0, (control, rows[0])
+        bytes_of[control] = float(rows[0]["bytes_total"])
+    nnz = float(rows[0]["nnz"])
+    assert bytes_of["wide"] == pytest.approx(bytes_of["lane"] + 2 * nnz)
