@@ -704,8 +704,15 @@ constexpr int kGathers = SPMV_TILE_GATHERS;
 template <class V>
 struct DenseResidency { static constexpr int value = sizeof(V) == 8 ? 3 : 4; };
 
+// Rows go to the groups of P threads from group `rotation` on (row i of the tile to group (rotation + i) mod
+// groups, a pass of `groups` rows at a time); returns the tile's rows. The caller advances the rotation by
+// each tile's rows, so that a tile with fewer rows than groups leaves different warps idle each time and
+// every warp takes its share of the rows (otherwise the last warps of the CTA would never get a row and
+// sit idle for the whole launch, e.g. 27-point stencil T = 8 on one thread per row: about 189 rows a tile
+// for 256 groups).
 template <class V, int LAYOUT, int T, int P, int W>
-__device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned char* stage, const StagePlan& plan) {
+__device__ __forceinline__ int process_tile(const KernelArgs& a, const unsigned char* stage, const StagePlan& plan,
+                                            int rotation) {
   using VT = ValueTraits<V>;
   constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
   constexpr int S = T / P;
@@ -718,9 +725,10 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
   V* y = static_cast<V*>(a.y);
   const uint64_t keep = l2_keep_policy();
   const int group = threadIdx.x / P, p = threadIdx.x % P;
+  const int slot = group >= rotation ? group - rotation : group - rotation + kGroups;
 
   for (int first = 0; first < tile.rows; first += kGroups) {
-    const int local = first + group;
+    const int local = first + slot;
     const int row = tile.row_begin + local;
     const bool active = local < tile.rows;
     if constexpr (!kPacked) {
@@ -790,6 +798,7 @@ __device__ __forceinline__ void process_tile(const KernelArgs& a, const unsigned
       }
     }
   }
+  return tile.rows;
 }
 
 // Thread 0: streams tile `tile_id` into a stage and arms its full barrier with the byte count.
@@ -1220,6 +1229,7 @@ __global__ void __launch_bounds__(kTileBlock, W) k_spmv_tiles(const KernelArgs a
   }
   __syncthreads();
 
+  int rotation = 0;   // the first group of the next tile's rows
   for (int64_t k = 0; k < my_tiles; ++k) {
     const int s = (int)(k % stages);
     if (!mbarrier_wait_bounded(full0 + 8 * s, (uint32_t)((k / stages) & 1), 2000000000ull)) {
@@ -1228,7 +1238,8 @@ __global__ void __launch_bounds__(kTileBlock, W) k_spmv_tiles(const KernelArgs a
     }
     // leave together or not at all: the reduction's shuffles need every lane of the warp
     if (__shfl_sync(0xffffffffu, *(volatile int*)&s_abort, 0)) break;
-    process_tile<V, LAYOUT, T, P, W>(a, buffers + s * plan.bytes, plan);
+    const int rows = process_tile<V, LAYOUT, T, P, W>(a, buffers + s * plan.bytes, plan, rotation);
+    rotation = (rotation + rows) % (kTileBlock / P);
     __syncwarp();
     if ((threadIdx.x & 31) == 0) {
       __threadfence_block();   // this warp's reads of the buffer happen before its release

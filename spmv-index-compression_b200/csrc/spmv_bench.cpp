@@ -360,6 +360,10 @@ void run_precision(spmv_csr* matrix, const std::string& name, int dtype, const A
       if (ms < best_ms) { best_ms = ms; best_tpr = tpr; best_batch = batch; }
     }
     check(spmv_memory_of(matrix, &facts, layout.code, dtype, best_tpr > 0 ? best_tpr : 8, &row.memory), "memory_of");
+    if (layout.code == SPMV_LAYOUT_R16 && r16_control_code(args.r16_control) == SPMV_R16_CONTROL_WIDE) {
+      row.memory.total += (double)info.nnz * 2;
+      row.memory.columns = (double)info.nnz * 4;
+    }
     if (samples.empty()) {
       row.status = "not admissible";
       append(args.csv, Row::header(), row.csv());
