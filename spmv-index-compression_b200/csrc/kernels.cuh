@@ -1172,9 +1172,21 @@ __device__ __forceinline__ bool run_segment(const KernelArgs& a, int64_t& block)
 }
 
 // Blocks [0, long_blocks): one long row each; then the segments from P = 32 down to P = 1; then short rows.
+// ---- programmatic dependent launch -------------------------------------------------------------------
+// The product kernels are launched with programmatic stream serialization: each CTA lets the next kernel of
+// the stream be scheduled as soon as every CTA of this grid has started, and that kernel's CTAs take the
+// multiprocessors this grid's CTAs leave while it finishes. Before it reads x or writes y, a CTA waits
+// until the previous kernel of the stream has completed and its memory is visible (griddepcontrol.wait
+// returns at once when there is no such kernel, or when it never let its dependents start early: every
+// other kernel of the library, the copies and the collectives keep the full stream order).
+__device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void wait_for_previous_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 template <class V, int LAYOUT, int T>
 __global__ void __launch_bounds__(kTileBlock, 4) k_spmv_classes(const KernelArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
+  allow_next_grid();
+  wait_for_previous_grid();
   int64_t block = blockIdx.x;
   if (block < a.long_blocks) {
     long_rows<V, LAYOUT, T>(a, smem, block, a.long_blocks);
@@ -1198,7 +1210,9 @@ __global__ void __launch_bounds__(kTileBlock, W) k_spmv_tiles(const KernelArgs a
   static_assert(T % P == 0 && P >= 1 && P <= 32, "P must divide T");
   constexpr int kWarps = kTileBlock / 32;
   extern __shared__ __align__(128) unsigned char smem[];
+  allow_next_grid();
   if ((int64_t)blockIdx.x < a.vector_blocks) {   // rows longer than a tile, scheduled first
+    wait_for_previous_grid();
     long_rows<V, LAYOUT, T>(a, smem, blockIdx.x, a.vector_blocks);
     publish_peer_rows(a);
     return;
@@ -1214,6 +1228,9 @@ __global__ void __launch_bounds__(kTileBlock, W) k_spmv_tiles(const KernelArgs a
   const uint32_t full0 = smem_address(smem);
   unsigned char* buffers = smem + 64;
 
+  // the first buffers' copies read only the matrix, so they are issued before the wait for the previous
+  // kernel; a tile that stages a window of x reads x, so with windows the wait comes first
+  if (a.tile_windows) wait_for_previous_grid();
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int s = 0; s < stages; ++s) {
@@ -1227,6 +1244,7 @@ __global__ void __launch_bounds__(kTileBlock, W) k_spmv_tiles(const KernelArgs a
       s_fills[s] = 1;
     }
   }
+  wait_for_previous_grid();
   __syncthreads();
 
   int rotation = 0;   // the first group of the next tile's rows

@@ -5,13 +5,29 @@
 namespace spmvb200 {
 namespace {
 
+// A product kernel launched so that it may start while the previous kernel of the stream finishes (it
+// waits for that kernel before it reads x or writes y; see allow_next_grid / wait_for_previous_grid).
+template <class Kernel>
+cudaError_t launch_product(Kernel kernel, int64_t blocks, int smem, cudaStream_t stream, const KernelArgs& a) {
+  cudaLaunchConfig_t config{};
+  config.gridDim = dim3((unsigned)blocks);
+  config.blockDim = dim3(kTileBlock);
+  config.dynamicSmemBytes = (size_t)smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  return cudaLaunchKernelEx(&config, kernel, a);
+}
+
 template <class V, int L, int T, int P, int W>
 cudaError_t run_tiles(const KernelArgs& a, cudaStream_t stream) {
   const int smem = a.smem_bytes;
   const int64_t blocks = a.vector_blocks + a.tile_ctas;
   if (blocks <= 0) return cudaSuccess;
-  k_spmv_tiles<V, L, T, P, W><<<(unsigned)blocks, kTileBlock, smem, stream>>>(a);
-  return cudaGetLastError();
+  return launch_product(k_spmv_tiles<V, L, T, P, W>, blocks, smem, stream, a);
 }
 
 // Sets the shared-memory limit of the variant to smem and returns its resident CTAs per multiprocessor.
@@ -94,8 +110,7 @@ template <class V, int L, int T>
 cudaError_t classes_variant(int mode, const KernelArgs& a, int64_t blocks, int smem, cudaStream_t stream) {
   if (mode == 1) return cudaFuncSetAttribute(k_spmv_classes<V, L, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (blocks <= 0) return cudaSuccess;
-  k_spmv_classes<V, L, T><<<(unsigned)blocks, kTileBlock, smem, stream>>>(a);
-  return cudaGetLastError();
+  return launch_product(k_spmv_classes<V, L, T>, blocks, smem, stream, a);
 }
 
 template <class V, int L>
