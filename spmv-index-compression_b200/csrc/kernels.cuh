@@ -121,6 +121,10 @@ struct KernelArgs {
   int window_elements;       // x elements a tile's window holds at most
   int stages;                // shared-memory buffers of a tile CTA (1..kMaxStages)
   const int* row_list;       // rows of the vector path (nullptr: rows 0..row_count-1)
+  // CSR-lp long rows: lane L's column after each kLaneMarkEvery of its deltas, [(j - 1) * T + L] for the
+  // j-th mark of the row_list item's row, from lane_mark_first[item] on
+  const int* lane_marks;
+  const int64_t* lane_mark_first;
   int64_t row_count;         // entries of row_list, or rows
   int64_t vector_blocks;     // k_spmv_tiles: its first vector_blocks CTAs take the rows of row_list
   int long_chunk;            // k_spmv_tiles: entries per chunk of a long row (a multiple of kTileBlock)
@@ -865,15 +869,18 @@ __device__ __forceinline__ void issue_tile(const KernelArgs& a, int64_t tile_id,
 // ---- rows longer than a tile ----------------------------------------------------------------------------
 // A row of the long-row list takes a whole CTA, chunk by chunk (a chunk starts at a multiple of T within
 // the row, so an entry keeps its lane), with the warps specialised. Warp 0 consumes: its T lane owners
-// add a chunk into their lane sums in order. The gatherers (warps 1..7; warps 2..7 for CSR-lp) fill one of
-// two shared-memory buffers per chunk with the chunk's values and x gathered at its columns. For CSR-lp,
-// warp 1 decodes: its T lane owners decode their lanes' columns of the chunk into one of two column
-// buffers, a chunk ahead of the gatherers. Named barriers hand the buffers over (ids 1..8, see below);
-// every thread walks the same rows and chunks, so every barrier completes. The lane sums finish in the
-// width-T shuffle tree of warp 0.
-__host__ __device__ inline int long_smem_bytes(int chunk, int value_bytes, bool packed) {
-  return 4 * chunk * value_bytes + (packed ? 8 * chunk : 0);
-}
+// add a chunk into their lane sums in order. The gatherers (warps 1..7) fill one of two shared-memory
+// buffers per chunk with the chunk's values and x gathered at its columns. For CSR-lp each gatherer decodes
+// the columns it gathers: a segment of kLaneMarkEvery deltas of one lane from that lane's column mark, the
+// lanes of a segment on neighbouring threads (so that their values are read together). Named barriers hand
+// the buffers over (ids 1..4, see below); every thread walks the same rows and chunks, so every barrier
+// completes. The lane sums finish in the width-T shuffle tree of warp 0.
+__host__ __device__ inline int long_smem_bytes(int chunk, int value_bytes) { return 4 * chunk * value_bytes; }
+
+// CSR-lp long rows: a lane's deltas in segments of this many, each decoded on its own from the lane's
+// column mark before it (the marks come from the matrix's columns when the operator is created). A chunk
+// holds whole segments of every lane: its entries are a multiple of kLaneMarkEvery * T.
+constexpr int kLaneMarkEvery = 16;
 
 // Named barriers with immediate ids, so that the kernel reserves only the barriers it uses.
 template <int ID, int THREADS>
@@ -902,20 +909,19 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
   using Index = typename LayoutTraits<LAYOUT>::Index;
   constexpr bool kPacked = LAYOUT == SPMV_LAYOUT_LP;
   constexpr bool kBase = LayoutTraits<LAYOUT>::kBase;
-  constexpr int kFirstGatherer = kPacked ? 64 : 32;          // warp 1 decodes for CSR-lp
+  constexpr int kFirstGatherer = 32;
   constexpr int kGatherers = kTileBlock - kFirstGatherer;
   using Full = BarrierPair<1, kGatherers + 32>;              // gatherers arrive, the consumer waits
   using Free = BarrierPair<3, kGatherers + 32>;              // the consumer arrives, gatherers wait
-  using Decoded = BarrierPair<5, kGatherers + 32>;           // CSR-lp: the decoder arrives, gatherers wait
-  using Read = BarrierPair<7, kGatherers + 32>;              // CSR-lp: gatherers arrive, the decoder waits
-  const int chunk = a.long_chunk;   // entries per chunk: a multiple of kTileBlock (and so of T)
-  if (long_smem_bytes(chunk, (int)sizeof(V), kPacked) > a.smem_bytes) {   // never by construction
+  // entries per chunk: a multiple of kTileBlock (and so of T), for CSR-lp of kLaneMarkEvery * T as well
+  const int chunk = a.long_chunk;
+  if (long_smem_bytes(chunk, (int)sizeof(V)) > a.smem_bytes ||
+      (kPacked && chunk % (kLaneMarkEvery * T) != 0)) {   // never by construction
     if (threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusSmem);
     return;
   }
   V* const s_values = reinterpret_cast<V*>(smem);                    // [2][chunk]
   V* const s_x = s_values + 2 * chunk;                                // [2][chunk]
-  int* const s_columns = reinterpret_cast<int*>(s_x + 2 * chunk);     // CSR-lp: [2][chunk]
   const V* values = static_cast<const V*>(a.values);
   const V* x = static_cast<const V*>(a.x);
   const Index* index = static_cast<const Index*>(a.columns);
@@ -948,45 +954,6 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
         static_cast<V*>(a.y)[row] = result;
         mirror_row(a, row, result);
       }
-    } else if (kPacked && warp == 1) {   // CSR-lp decoder
-      const int quotient = (int)(length / T), remainder = (int)(length - (int64_t)quotient * T);
-      const uint32_t width = a.row_width[row];
-      const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
-      const uint32_t* words = a.words + a.row_word[row];
-      uint64_t bit = lane < T ? (uint64_t)width * (uint64_t)(lane * quotient + (lane < remainder ? lane : remainder)) : 0;
-      int column = a.row_base[row];
-      for (int k = 0; k < chunks; ++k) {
-        const int b = k & 1, count = count_of(k);
-        if (k >= 2) Read::sync(b);   // the gatherers are done with the columns of chunk k - 2
-        int* columns = s_columns + b * chunk;
-        if (lane < T) {
-          // the words of every delta first (their positions do not depend on the decode), 8 at a time,
-          // then the running column
-          int i = lane;
-          for (; i + 7 * T < count; i += 8 * T) {
-            uint32_t delta[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint64_t at = bit + (uint64_t)k * width;
-              const uint64_t w = at >> 5;
-              delta[k] = __funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1), (uint32_t)(at & 31)) & mask;
-            }
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              column += (int)delta[k];
-              columns[i + k * T] = column;
-            }
-            bit += 8 * (uint64_t)width;
-          }
-          for (; i < count; i += T, bit += width) {
-            const uint64_t w = bit >> 5;
-            column += (int)(__funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1), (uint32_t)(bit & 31)) & mask);
-            columns[i] = column;
-          }
-        }
-        Decoded::arrive(b);
-      }
-      for (int k = chunks >= 2 ? chunks - 2 : 0; k < chunks; ++k) Read::sync(k & 1);
     } else {   // gatherers
       const int gatherer = (int)threadIdx.x - kFirstGatherer;
       const int base = kBase ? a.row_base[row] : 0;
@@ -994,18 +961,58 @@ __device__ __forceinline__ void long_rows(const KernelArgs& a, unsigned char* sm
       for (int k = 0; k < chunks; ++k) {
         const int b = k & 1, count = count_of(k);
         if (k >= 2) Free::sync(b);   // the consumer is done with chunk k - 2
-        const int* columns = s_columns + b * chunk;
-        if constexpr (kPacked) Decoded::sync(b);
         const int64_t first = begin + (int64_t)k * chunk;
         V* v = s_values + b * chunk;
         V* g = s_x + b * chunk;
+        if constexpr (kPacked) {
+          // task t: lane t % T, segment t / T of the chunk's segments (deltas d0 .. d0 + K - 1 of the lane)
+          constexpr int K = kLaneMarkEvery;
+          const int quotient = (int)(length / T), remainder = (int)(length - (int64_t)quotient * T);
+          const uint32_t width = a.row_width[row];
+          const uint32_t mask = width == 0 ? 0u : (0xffffffffu >> (32 - width));
+          const uint32_t* words = a.words + a.row_word[row];
+          const int* marks = a.lane_marks + a.lane_mark_first[item];
+          const int per_lane = chunk / T;
+          for (int t = gatherer; t < (per_lane / K) * T; t += kGatherers) {
+            const int lane_of = t % T;
+            const int d0 = k * per_lane + (t / T) * K;
+            const int n = quotient + (lane_of < remainder ? 1 : 0) - d0;   // deltas of the lane from d0 on
+            if (n <= 0) continue;
+            int column = d0 == 0 ? base : marks[(d0 / K - 1) * T + lane_of];
+            const uint64_t bit0 =
+                (uint64_t)width * (uint64_t)(lane_of * quotient + (lane_of < remainder ? lane_of : remainder) + d0);
+            const int64_t e0 = (int64_t)lane_of + (int64_t)d0 * T - (int64_t)k * chunk;   // chunk entry of d0
+#pragma unroll
+            for (int h = 0; h < K; h += 8) {
+              // the words of 8 deltas first (their positions do not depend on the decode), then the
+              // running column, the values and the gathers
+              uint32_t delta[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                if (h + j < n) {
+                  const uint64_t at = bit0 + (uint64_t)(h + j) * width;
+                  const uint64_t w = at >> 5;
+                  delta[j] = __funnelshift_r(load_readonly(words + w), load_readonly(words + w + 1),
+                                             (uint32_t)(at & 31)) & mask;
+                }
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                if (h + j < n) {
+                  column += (int)delta[j];
+                  const int i = (int)(e0 + (int64_t)(h + j) * T);
+                  v[i] = load_stream(values + first + i, stream);
+                  g[i] = load_x(x + column, keep);
+                }
+            }
+          }
+        } else {
 #pragma unroll 8
-        for (int i = gatherer; i < count; i += kGatherers) {
-          const int c = kPacked ? columns[i] : base + (int)load_stream(index + first + i, stream);
-          v[i] = load_stream(values + first + i, stream);
-          g[i] = load_x(x + c, keep);
+          for (int i = gatherer; i < count; i += kGatherers) {
+            const int c = base + (int)load_stream(index + first + i, stream);
+            v[i] = load_stream(values + first + i, stream);
+            g[i] = load_x(x + c, keep);
+          }
         }
-        if constexpr (kPacked) Read::arrive(b);
         Full::arrive(b);
       }
       // the next row refills the buffers: wait until the consumer has released the last ones

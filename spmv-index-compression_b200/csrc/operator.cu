@@ -213,6 +213,27 @@ struct ClassPlan {
   std::vector<int> long_rows;
 };
 
+// CSR-lp long rows: lane L's column after each kLaneMarkEvery of its deltas, which is the column of its
+// entry L + (j * kLaneMarkEvery - 1) * T for the j-th mark (0 where the lane has no such entry), j = 1 ..
+// ceil(ceil(length / T) / kLaneMarkEvery) - 1, at [first[item] + (j - 1) * T + L].
+void build_lane_marks(const Csr& matrix, const std::vector<int>& long_rows, int tpr, std::vector<int>& marks,
+                      std::vector<int64_t>& first) {
+  marks.clear();
+  first.assign(long_rows.size(), 0);
+  for (size_t item = 0; item < long_rows.size(); ++item) {
+    const int row = long_rows[item];
+    const int64_t begin = matrix.row_ptr[row], length = (int64_t)matrix.row_ptr[row + 1] - begin;
+    const int64_t per_lane = (length + tpr - 1) / tpr;
+    const int64_t count = (per_lane + kLaneMarkEvery - 1) / kLaneMarkEvery - 1;
+    first[item] = (int64_t)marks.size();
+    for (int64_t j = 1; j <= count; ++j)
+      for (int lane = 0; lane < tpr; ++lane) {
+        const int64_t entry = lane + (j * kLaneMarkEvery - 1) * tpr;
+        marks.push_back(entry < length ? matrix.col_ind[(size_t)(begin + entry)] : 0);
+      }
+  }
+}
+
 ClassPlan plan_classes(const Csr& matrix, int tpr, int long_threshold) {
   ClassPlan plan;
   std::vector<int4> segments[6];
@@ -258,6 +279,8 @@ struct spmv_operator {
   int4* tiles = nullptr;
   int2* tile_words = nullptr;
   int* long_rows = nullptr;
+  int* lane_marks = nullptr;           // CSR-lp long rows (build_lane_marks)
+  int64_t* lane_mark_first = nullptr;
   unsigned* status = nullptr;
   int64_t tile_count = 0;
   int64_t tile_ctas = 0;
@@ -283,7 +306,8 @@ struct spmv_operator {
     cudaGetDevice(&previous);
     if (previous != device) cudaSetDevice(device);
     for (void* pointer : {(void*)row_ptr, values, columns, (void*)row_base, (void*)row_word, (void*)row_width,
-                          (void*)words, (void*)tiles, (void*)tile_words, (void*)long_rows, (void*)status,
+                          (void*)words, (void*)tiles, (void*)tile_words, (void*)long_rows, (void*)lane_marks,
+                          (void*)lane_mark_first, (void*)status,
                           (void*)row_items, (void*)tile_windows})
       if (pointer) cudaFree(pointer);
     if (previous >= 0 && previous != device) cudaSetDevice(previous);
@@ -293,6 +317,15 @@ struct spmv_operator {
 using namespace spmvb200;
 
 namespace {
+
+void upload_lane_marks(spmv_operator* op, const Csr& m, const std::vector<int>& long_rows, int tpr) {
+  std::vector<int> marks;
+  std::vector<int64_t> first;
+  build_lane_marks(m, long_rows, tpr, marks, first);
+  op->lane_marks = device_upload<int>(marks.empty() ? nullptr : marks.data(), std::max<size_t>(marks.size(), 1),
+                                      op->device_bytes);
+  op->lane_mark_first = device_upload<int64_t>(first.data(), first.size(), op->device_bytes);
+}
 
 KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   KernelArgs a{};
@@ -321,6 +354,8 @@ KernelArgs kernel_args(const spmv_operator* op, const void* x, void* y) {
   a.dense = op->dense ? 1 : 0;
   a.row_list = op->long_rows;
   a.row_count = op->long_count;
+  a.lane_marks = op->lane_marks;
+  a.lane_mark_first = op->lane_mark_first;
   a.vector_blocks = op->long_ctas;
   a.long_chunk = op->long_chunk;
   a.smem_bytes = op->smem_bytes;
@@ -532,8 +567,10 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
       op->long_count = (int64_t)plan.long_rows.size();
       op->row_items = device_upload<int4>(plan.items.data(), plan.items.size(), op->device_bytes);
       op->long_rows = device_upload<int>(plan.long_rows.data(), plan.long_rows.size(), op->device_bytes);
-      op->long_chunk = value_bytes == 8 ? 1024 : 2048;
-      op->smem_bytes = op->long_count > 0 ? long_smem_bytes(op->long_chunk, value_bytes, layout == SPMV_LAYOUT_LP) : 0;
+      // (CSR-lp with 2-byte values: 3584 = 224 * 16, a chunk of exactly one 16-delta segment per gatherer)
+      op->long_chunk = value_bytes == 8 ? 1024 : (layout == SPMV_LAYOUT_LP && value_bytes == 2 ? 3584 : 2048);
+      op->smem_bytes = op->long_count > 0 ? long_smem_bytes(op->long_chunk, value_bytes) : 0;
+      if (layout == SPMV_LAYOUT_LP && op->long_count > 0) upload_lane_marks(op.get(), m, plan.long_rows, tpr);
       int64_t blocks = op->long_count;
       for (int segment = 0; segment < 6; ++segment) {
         const int per_block = kTileBlock >> segment;
@@ -615,11 +652,13 @@ int spmv_operator_create(const spmv_csr* matrix, const spmv_operator_config* con
     if (layout == SPMV_LAYOUT_LP)
       op->tile_words = device_upload<int2>(plan.tile_words.data(), plan.tile_words.size(), op->device_bytes);
     op->long_rows = device_upload<int>(plan.long_rows.data(), plan.long_rows.size(), op->device_bytes);
-    // long rows: one CTA per row at a time; a chunk of a long row (values, gathered x and, for CSR-lp,
-    // decoded columns) lives in the CTA's shared memory, at least kTileBlock entries, at most 8192, and
+    // long rows: one CTA per row at a time; a chunk of a long row (values and gathered x) lives in the
+    // CTA's shared memory, at least kTileBlock entries (CSR-lp: and whole lane segments), at most 8192, and
     // the launch gets the larger of the tile buffers and one chunk
-    op->long_chunk = std::max(kTileBlock, std::min(8192, (smem / long_smem_bytes(1, value_bytes, packed)) / kTileBlock * kTileBlock));
-    op->smem_bytes = std::max(smem, op->long_count > 0 ? long_smem_bytes(op->long_chunk, value_bytes, packed) : 0);
+    const int chunk_unit = packed ? std::max(kTileBlock, kLaneMarkEvery * tpr) : kTileBlock;
+    op->long_chunk = std::max(chunk_unit, std::min(8192, (smem / long_smem_bytes(1, value_bytes)) / chunk_unit * chunk_unit));
+    op->smem_bytes = std::max(smem, op->long_count > 0 ? long_smem_bytes(op->long_chunk, value_bytes) : 0);
+    if (packed && op->long_count > 0) upload_lane_marks(op.get(), m, plan.long_rows, tpr);
     if (op->smem_bytes > shared_limit) fail(SPMV_ERR_INVALID_ARGUMENT, "long-row chunk exceeds the shared memory of a block");
     // persistent tile CTAs: as many as fit on the device at once, never more than there are tiles
     const int resident = tiles_occupancy(kernel, layout, tpr, op->physical_tpr, op->smem_bytes, op->dense);
