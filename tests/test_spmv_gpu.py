@@ -372,3 +372,28 @@ def test_block_rows_of_column_runs(dtype):
                 assert op.info().physical_tpr == 8 and op.info().tile_rows == 64
             y = device_run(op, x)
         assert np.array_equal(bits(y), bits(oracle_product(matrix, x, dtype, layout, tpr))), (spmv.LAYOUT_NAMES[layout], tpr)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_long_rows_on_the_class_schedule_at_segment_and_chunk_edges(dtype):
+    """Rows above 64*T entries run one CTA each; for CSR-lp every gatherer decodes 16 deltas of one lane from
+    that lane's column mark. Lengths just around 16*T*k and around the class chunk (1024, 2048 or 3584 entries)
+    leave lanes with fewer deltas than a segment, segments cut by the row's end and rows over several chunks;
+    every layout must give the oracle's CSR-i32 bits."""
+    for tpr in spmv.THREADS_PER_ROW:
+        chunk = {spmv.F64: 1024, spmv.F32: 2048, spmv.F16: 3584}[dtype]
+        lengths = [64 * tpr + 1, 16 * tpr * 5 - 1, 16 * tpr * 5 + 1, chunk - 1, chunk + 1, 3 * chunk + 16 * tpr - 3,
+                   7 * tpr + 64 * tpr + 5]
+        rows, cols = 400, 12000
+        long_rows = {5 + 37 * i: n for i, n in enumerate(lengths)}
+        row_ptr, col_ind, values = random_csr(rows, cols, lambda rng: rng.integers(0, 12), 41 + tpr, empty_every=13,
+                                              long_rows=long_rows)
+        matrix = spmv.CsrMatrix.from_arrays(rows, cols, row_ptr, col_ind, values, name="long-edges")
+        x = spmv.fill_uniform(dtype, cols, 3)
+        expected = oracle_product(matrix, x, dtype, spmv.I32, tpr)
+        for layout in (spmv.I32, spmv.LP):
+            with spmv.Operator(matrix, layout, dtype, tpr, schedule=spmv.SCHEDULE_CLASSES) as op:
+                assert op.info().long_rows == sum(n > 64 * tpr for n in lengths), (tpr, op.info().long_rows)
+                y = device_run(op, x)
+                op.check()
+            assert np.array_equal(bits(y), bits(expected)), (spmv.LAYOUT_NAMES[layout], tpr)
