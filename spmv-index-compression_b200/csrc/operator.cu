@@ -10,9 +10,12 @@
 //   tiles     int4[tiles]                         {row_begin, row_end, entry_begin, entry_end}
 //   tile_words int2[tiles]                        lp: {first word, last word + 1} of each tile's stream
 //   long_rows int32[long_rows]                    rows longer than a tile
+//   lane_marks int32[...], lane_mark_first int64[long_rows]
+//                                                 lp long rows: each lane's column after every 16 deltas
 //   status    uint32                              bit 0: a bounded device wait gave up
 // The streams are the reference's (bench_csr_width.cu:795-951), so memory_of counts them exactly; the
-// tile plan adds 16 bytes per tile (about 2048 nonzeros) and 4 bytes per long row.
+// tile plan adds 16 bytes per tile (about 2048 nonzeros) and 4 bytes per long row, and CSR-lp 4 bytes per 16
+// entries of its long rows.
 #include <cuda_runtime.h>
 #include <climits>
 
